@@ -1,0 +1,131 @@
+/*
+ * ltxfp8 -- C ABI of the B200 (sm_100a) blockwise-FP8 linear layer.
+ *
+ * Plain pointers and sizes only.  Every device pointer is a CUDA device
+ * address on the current device; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  No entry point allocates device memory or synchronises the
+ * stream, so every call can be enqueued inside CUDA-graph capture.  Each call
+ * returns LTXFP8_OK (0) or a negative error code; ltxfp8_last_error() gives a
+ * human-readable message for the calling thread.
+ *
+ * Layouts (those of Lightricks/LTX-2's ltx-kernels blockwise path):
+ *   activations  bf16 [M, K] row-major (K contiguous)
+ *   act codes    e4m3fn [M, K] row-major
+ *   act scales   fp32, MN-major: scale of (row m, K-block kb) at sfa[kb * sfa_ld + m],
+ *                sfa_ld >= M (the reference uses align4(M))
+ *   weights      e4m3fn [N, K] row-major; scales fp32 [N/128, K/128] row-major
+ *   bias         fp32 [N] or NULL
+ *   output       bf16 [M, N] row-major
+ */
+#ifndef LTXFP8_H
+#define LTXFP8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LTXFP8_OK 0
+#define LTXFP8_ERR_INVALID_ARGUMENT (-1)
+#define LTXFP8_ERR_UNSUPPORTED_SHAPE (-2)
+#define LTXFP8_ERR_MISALIGNED (-3)
+#define LTXFP8_ERR_CUDA (-4)
+#define LTXFP8_ERR_DEVICE (-5)       /* wrong architecture or no device */
+#define LTXFP8_ERR_DEVICE_STATUS (-6) /* a kernel recorded a bounded-wait timeout */
+
+/* Activation-quantisation modes (flags of ltxfp8_quantize_1x128). */
+#define LTXFP8_QUANT_TORCH 0  /* s = (1/amax)*448, IEEE roundings: bit-exact with blockwise_quantize_torch */
+#define LTXFP8_QUANT_TRITON 1 /* s = 448/amax, 1/s via div.full.f32: the arithmetic of the Triton kernel */
+
+/* Input dtypes for ltxfp8_quantize_weight_128x128. */
+#define LTXFP8_DTYPE_F32 0
+#define LTXFP8_DTYPE_BF16 1
+#define LTXFP8_DTYPE_F16 2
+
+/* Library version, (major << 16) | minor. */
+int ltxfp8_version(void);
+
+/* Message for the last error returned on the calling thread ("" if none). */
+const char* ltxfp8_last_error(void);
+
+/*
+ * Per-token 1x128 activation quantisation.
+ *   x      bf16 [M, K], row stride x_ld elements (x_ld >= K, x_ld % 8 == 0)
+ *   q      e4m3 [M, K], row stride q_ld bytes (q_ld % 8 == 0)
+ *   sfa    fp32, element (m, kb) at sfa[kb * sfa_ld + m], sfa_ld >= M
+ *   K % 128 == 0.  flags: LTXFP8_QUANT_TORCH or LTXFP8_QUANT_TRITON.
+ * Replaces the Triton op blockwise::quantize with use_gelu=False
+ * (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:128-151, kernel :102-126)
+ * and blockwise_quantize_torch (functional.py:138-144).
+ */
+int ltxfp8_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld, float* sfa,
+                          int64_t sfa_ld, int flags, void* stream);
+
+/*
+ * 128x128 block weight quantisation: w [N, K] (dtype LTXFP8_DTYPE_*) ->
+ * q e4m3 [N, K] and sfb fp32 [N/128, K/128].  N % 128 == 0, K % 128 == 0.
+ * Replaces blockwise_quantize_weights
+ * (ltx-kernels/src/ltx_kernels/blockwise/functional.py:128-135).
+ */
+int ltxfp8_quantize_weight_128x128(const void* w, int dtype, int64_t N, int64_t K, void* q, float* sfb,
+                                   void* stream);
+
+/*
+ * 1x128 dequantisation: out[m, k] = bf16(e4m3(q[m, k]) * scales[m * row_stride + (k/128) * col_stride]).
+ * K % 128 == 0.  Replaces blockwise::dequantize
+ * (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:387-433).
+ */
+int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stride, int64_t col_stride, int64_t M,
+                            int64_t K, void* out, void* stream);
+
+/* Epilogue options of ltxfp8_gemm (all zero = plain bias + bf16 store). */
+typedef struct ltxfp8_epilogue {
+  int gelu_tanh;          /* apply GELU (tanh approximation) to bf16(acc + bias), rounding to bf16 */
+  void* requant_q;        /* non-NULL: write the 1x128 e4m3 quantisation of the bf16 result, [M, N] */
+  float* requant_scales;  /* its scales, element (m, nb) at requant_scales[nb * requant_ld + m] */
+  int64_t requant_ld;     /* >= M */
+  int skip_d;             /* non-zero: do not write D (only valid with requant_q) */
+  const void* lora_ax;    /* non-NULL: bf16 [M, lora_r], the LoRA down projection x A^T */
+  const void* lora_b;     /* bf16 [N, lora_r], the LoRA up projection */
+  int64_t lora_r;         /* rank, multiple of 16, <= 256 */
+  float lora_alpha;       /* scale of the LoRA term */
+} ltxfp8_epilogue;
+
+/*
+ * Blockwise-scaled FP8 GEMM (NT) with fused epilogue:
+ *   D = bf16( sum_kb sfa[m,kb] sfb[n/128,kb] (A W^T)_kb + alpha B (x A^T)^T + bias )
+ *   optionally followed by GELU-tanh and 1x128 requantisation.
+ * M >= 1, N % 128 == 0, K % 128 == 0 (any K, not only 2048/4096/8192/16384).
+ * ep may be NULL.
+ * Replaces blockwise_cpp.fp8_gemm_nt_sm89 (ltx-kernels/csrc/blockwise/api.cpp:42-65,
+ * sm89_fp8_gemm_1d2d.hpp:17-37, kernels/geforce/gemm.cu:256-275) and the
+ * unfused F.gelu + requant of the FFN (ltx-core/.../gelu_approx.py:10,
+ * ltx-kernels/.../linear.py:91-93).
+ */
+int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
+                void* stream);
+
+/*
+ * LoRA down projection: ax bf16 [M, r] = x bf16 [M, K] . lora_a bf16 [r, K]^T (fp32 accumulation).
+ * K % 64 == 0, r % 16 == 0, 16 <= r <= 256.  No reference counterpart: the
+ * reference merges LoRA into the weights at load time
+ * (ltx-core/src/ltx_core/quantization/blockwise/_impl.py:277-301); this is the
+ * runtime form of that term.
+ */
+int ltxfp8_lora_a(const void* x, const void* lora_a, void* ax, int64_t M, int64_t K, int64_t r, void* stream);
+
+/*
+ * Read (and optionally clear) the device status word that kernels set when a
+ * bounded wait gives up.  Synchronises the given stream.  *status = 0 means
+ * no kernel has failed since the last clear.
+ */
+int ltxfp8_device_status(unsigned int* status, int clear, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LTXFP8_H */

@@ -1,0 +1,355 @@
+// Blockwise-scaled FP8 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   D[m, n] = bf16( sum_kb sfa[m, kb] * sfb[n/128, kb] * (A[m, kb] . W[n, kb]) + bias[n] )
+//
+// A e4m3 [M, K] and W e4m3 [N, K] are K-contiguous ("NT"); sfa is MN-major
+// (element (m, kb) at sfa[kb * sfa_ld + m]); sfb is [N/128, K/128] row-major.
+// This is the contract of the reference's fp8_gemm_nt_sm89
+// (ltx-kernels/csrc/blockwise/api.cpp:42-65, kernels/geforce/gemm.cu:26-275).
+//
+// Design (one CTA per SM, persistent over 128 x 256 output tiles):
+//   warp 0      TMA producer: one 128-wide K block of A (16 KB) and W (32 KB)
+//               per pipeline stage, 4 stages, 128 B swizzle.
+//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (M128 N256 K32) per K
+//               block into one of two 256-column TMEM buffers, then
+//               tcgen05.commit to release the smem stage and hand the TMEM
+//               buffer to the epilogue.
+//   warps 4-11  promotion + epilogue: each thread owns one row and 128 columns.
+//               Per K block it reads the raw partial sums from TMEM and folds
+//               them into fp32 registers with the block's scale
+//               sfa[m,kb] * sfb[nb,kb] (the same promotion the reference does
+//               after every 128-K block, gemm.cu:185-199).  The two TMEM buffers
+//               let the tensor core run one K block ahead of the promotion.
+//               After the last block: + bias, optional GELU-tanh, optional
+//               1x128 requantisation to e4m3 for the next layer, stores.
+//   LoRA        alpha * (x A^T) B^T is folded in as extra K blocks of bf16 MMAs
+//               (kind::f16) over [x A^T | B], promoted with scale alpha.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace ltxfp8 {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 128;
+constexpr int kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK;               // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK;               // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;   // 48 KB
+constexpr int kGemmThreads = 384;
+constexpr uint32_t kTmemCols = 512;                   // 2 x 256 fp32 accumulator columns
+constexpr int kLoraChunk = 64;                        // bf16 K elements per LoRA block (128 B rows)
+constexpr uint32_t kGemmSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+// Register split between the producer/MMA warpgroup and the two epilogue
+// warpgroups; the launch must provide kGemmThreads * kGemmLaunchRegs.
+constexpr uint32_t kRegsCtrl = 56;
+constexpr uint32_t kRegsEpi = 224;
+constexpr uint32_t kGemmLaunchRegs = 168;
+static_assert(128 * kRegsCtrl + 256 * kRegsEpi <= kGemmThreads * kGemmLaunchRegs, "register split exceeds launch");
+
+enum GemmFlags : int {
+  kGemmBias = 1,     // add fp32 bias[n]
+  kGemmWriteD = 2,   // write the bf16 result (the GELU output when GELU is on)
+  kGemmLora = 4,     // extra bf16 K blocks with scale lora_alpha
+};
+
+// Device status codes recorded when a bounded wait gives up.
+enum GemmStatus : unsigned int {
+  kStProducerEmpty = 0x47010001u,
+  kStMmaTmemEmpty = 0x47010002u,
+  kStMmaFull = 0x47010003u,
+  kStEpiTmemFull = 0x47010004u,
+  kStDrain = 0x47010005u,
+};
+
+struct GemmParams {
+  int M, N, K;
+  int num_kb;         // K / 128
+  int num_lora;       // LoRA K blocks (ceil(r / 64)), 0 without LoRA
+  int m_tiles, n_tiles, group_m, total_tiles;
+  const float* sfa;
+  int64_t sfa_ld;
+  const float* sfb;   // [N/128, num_kb]
+  const float* bias;  // [N] fp32, may be null
+  __nv_bfloat16* d;   // [M, N]
+  uint8_t* q_out;     // [M, N] e4m3 (requant)
+  float* s_out;       // requant scales at s_out[nb * s_out_ld + m]
+  int64_t s_out_ld;
+  float lora_alpha;
+  int flags;
+};
+
+// Grouped rasterisation: consecutive tile indices walk group_m M-tiles down a
+// column of N-tiles, so the CTAs resident at one time share A and W tiles in L2.
+__device__ __forceinline__ void gemm_tile_coords(int tile, const GemmParams& p, int& mt, int& nt) {
+  const int per_group = p.group_m * p.n_tiles;
+  const int g = tile / per_group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.group_m, p.m_tiles - first_m);
+  const int r = tile - g * per_group;
+  mt = first_m + r % gm;
+  nt = r / gm;
+}
+
+template <bool kGelu, bool kRequant>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    fp8_blockwise_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                              const __grid_constant__ CUtensorMap tmLX, const __grid_constant__ CUtensorMap tmLB,
+                              const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;   // [2]
+  uint64_t* tempty = tfull + 2;        // [2]
+  uint64_t* drain = tempty + 2;        // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
+  const int lane = static_cast<int>(lane_id());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (p.num_lora > 0) {
+      tma_prefetch_desc(&tmLX);
+      tma_prefetch_desc(&tmLB);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_blocks = p.num_kb + p.num_lora;
+
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsCtrl>();
+    if (warp == 0 && lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        int mt, nt;
+        gemm_tile_coords(tile, p, mt, nt);
+        const int m0 = mt * kBM, n0 = nt * kBN;
+        for (int kb = 0; kb < num_blocks; ++kb, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, kStProducerEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          if (kb < p.num_kb) {
+            tma_load_2d(&tmA, &full[s], sa, kb * kBK, m0);
+            tma_load_2d(&tmB, &full[s], sb, kb * kBK, n0);
+          } else {
+            const int c = (kb - p.num_kb) * kLoraChunk;
+            tma_load_2d(&tmLX, &full[s], sa, c, m0);
+            tma_load_2d(&tmLB, &full[s], sb, c, n0);
+          }
+        }
+      }
+      if (!ok) {
+        // Let the loads already in flight land before the CTA exits.
+        const uint32_t first = it > static_cast<uint32_t>(kStages) ? it - kStages : 0u;
+        for (uint32_t i = first; i < it; ++i) mbar_wait(&full[i % kStages], (i / kStages) & 1u, kStDrain);
+      }
+    } else if (warp == 1 && lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t kIdescF8 = make_idesc(0u, kBM, kBN);
+      constexpr uint32_t kIdescBF16 = make_idesc(1u, kBM, kBN);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < num_blocks; ++kb, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+          const uint32_t buf = it & 1u, bph = (it >> 1) & 1u;
+          if (!mbar_wait(&tempty[buf], bph ^ 1u, kStMmaTmemEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          if (!mbar_wait(&full[s], ph, kStMmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t a_addr = smem_u32(smem + s * kStageBytes);
+          const uint64_t adesc = sw128_kmajor_desc(a_addr);
+          const uint64_t bdesc = sw128_kmajor_desc(a_addr + kABytes);
+          const uint32_t d_tmem = tmem_base + buf * kBN;
+          if (kb < p.num_kb) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)  // 4 x K32 (32 B of each 128 B row)
+              mma_f8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, kIdescF8, j > 0 ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)  // 4 x K16 bf16 (32 B of each 128 B row)
+              mma_f16(d_tmem, adesc + 2u * j, bdesc + 2u * j, kIdescBF16, j > 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&tfull[buf]);
+        }
+      }
+      // Every MMA this thread issued has completed once `drain` flips.
+      tc_commit(drain);
+      mbar_wait(drain, 0u, kStDrain);
+    }
+  } else {
+    setmaxnreg_inc<kRegsEpi>();
+    // -------------------------------------------------------------- promotion + epilogue
+    const int sp = warp & 3;          // TMEM sub-partition: rows 32*sp .. 32*sp+31
+    const int half = (warp - 4) >> 2; // which 128-column half of the 256-wide tile
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
+      int mt, nt;
+      gemm_tile_coords(tile, p, mt, nt);
+      const int row = mt * kBM + sp * 32 + lane;
+      const bool row_ok = row < p.M;
+      const int col0 = nt * kBN + half * 128;
+      const bool col_ok = col0 < p.N;  // N % 128 == 0: a 128-column slab is all in or all out
+      const int nb = col0 / 128;
+      const float* sfa_row = p.sfa + row;
+      const float* sfb_blk = p.sfb + static_cast<int64_t>(nb) * p.num_kb;
+
+      float acc[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+
+      // Scales are prefetched two K blocks ahead of their use.
+      float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+      if (row_ok) {
+        a0 = __ldg(sfa_row);
+        if (p.num_kb > 1) a1 = __ldg(sfa_row + p.sfa_ld);
+      }
+      if (col_ok) {
+        b0 = __ldg(sfb_blk);
+        if (p.num_kb > 1) b1 = __ldg(sfb_blk + 1);
+      }
+      for (int kb = 0; kb < num_blocks; ++kb, ++it) {
+        float a2 = 0.f, b2 = 0.f;
+        if (kb + 2 < p.num_kb) {
+          if (row_ok) a2 = __ldg(sfa_row + static_cast<int64_t>(kb + 2) * p.sfa_ld);
+          if (col_ok) b2 = __ldg(sfb_blk + kb + 2);
+        }
+        const float scale = kb < p.num_kb ? a0 * b0 : p.lora_alpha;
+        const uint32_t buf = it & 1u, bph = (it >> 1) & 1u;
+        // Warp-uniform outcome: the TMEM loads below are .sync.aligned.
+        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], bph, kStEpiTmemFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + buf * kBN + half * 128;
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(taddr + 0, r0);
+        tmem_ld_32x32b_x32(taddr + 32, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          acc[j] = fmaf(scale, __uint_as_float(r0[j]), acc[j]);
+          acc[32 + j] = fmaf(scale, __uint_as_float(r1[j]), acc[32 + j]);
+        }
+        tmem_ld_32x32b_x32(taddr + 64, r0);
+        tmem_ld_32x32b_x32(taddr + 96, r1);
+        tmem_wait_ld();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          acc[64 + j] = fmaf(scale, __uint_as_float(r0[j]), acc[64 + j]);
+          acc[96 + j] = fmaf(scale, __uint_as_float(r1[j]), acc[96 + j]);
+        }
+        a0 = a1; a1 = a2;
+        b0 = b1; b1 = b2;
+      }
+      if (!ok) break;
+      if (!(row_ok && col_ok)) continue;
+
+      // ------------------------------------------------ bias (+ GELU) in fp32, bf16 rounding
+      const bool has_bias = (p.flags & kGemmBias) != 0;
+      const float4* bias4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+      for (int c = 0; c < 128; c += 4) {
+        float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (has_bias) bv = __ldg(bias4 + c / 4);
+        acc[c] += bv.x;
+        acc[c + 1] += bv.y;
+        acc[c + 2] += bv.z;
+        acc[c + 3] += bv.w;
+      }
+      if constexpr (kGelu || kRequant) {
+        // The reference materialises bf16(acc + bias), applies GELU on that bf16
+        // tensor (result rounded to bf16) and quantises those bf16 values.
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          float y = bf16_round(acc[c]);
+          if constexpr (kGelu) y = bf16_round(gelu_tanh_f32(y));
+          acc[c] = y;
+        }
+      }
+      const int64_t out_off = static_cast<int64_t>(row) * p.N + col0;
+      if (p.flags & kGemmWriteD) {
+        uint4* dst = reinterpret_cast<uint4*>(p.d + out_off);
+#pragma unroll
+        for (int c = 0; c < 128; c += 8) {
+          dst[c / 8] = make_uint4(pack_bf16x2(acc[c], acc[c + 1]), pack_bf16x2(acc[c + 2], acc[c + 3]),
+                                  pack_bf16x2(acc[c + 4], acc[c + 5]), pack_bf16x2(acc[c + 6], acc[c + 7]));
+        }
+      }
+      if constexpr (kRequant) {
+        // One thread owns the whole 1x128 group of its row: no cross-thread reduction.
+        float amax = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) amax = fmax_nan(amax, fabsf(acc[c]));
+        const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
+        uint4* qdst = reinterpret_cast<uint4*>(p.q_out + out_off);
+#pragma unroll
+        for (int c = 0; c < 128; c += 16) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(acc[c + 4 * i], s), __fmul_rn(acc[c + 4 * i + 1], s));
+            const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(acc[c + 4 * i + 2], s), __fmul_rn(acc[c + 4 * i + 3], s));
+            w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+          }
+          qdst[c / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        p.s_out[static_cast<int64_t>(nb) * p.s_out_ld + row] = __frcp_rn(s);
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace ltxfp8

@@ -1,0 +1,356 @@
+// C-ABI entry points of the sm_100a blockwise-FP8 linear layer (include/ltxfp8.h).
+//
+// Host side: argument validation (the reference's TORCH_CHECK / Python asserts
+// become negative return codes), TMA tensor-map encoding, launch configuration.
+// Nothing here allocates device memory or synchronises a stream, except
+// ltxfp8_device_status which exists to read the device status word.
+#include "ltxfp8.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "gemm.cuh"
+#include "lora.cuh"
+#include "ptx.cuh"
+#include "quant.cuh"
+
+using namespace ltxfp8;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(LTXFP8_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D tensor map over a row-major [outer, inner] array, 128 B swizzle.
+int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(LTXFP8_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LTXFP8_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return LTXFP8_OK;
+}
+
+struct DeviceInfo {
+  bool init = false;
+  int sms = 0;
+  int major = 0, minor = 0;
+  bool gemm_ready[4] = {false, false, false, false};
+  bool lora_ready = false;
+};
+
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(LTXFP8_ERR_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    d.init = true;
+  }
+  if (d.major != 10 || d.minor != 0)
+    return fail(LTXFP8_ERR_DEVICE, "this library is built for sm_100a (B200); device %d is sm_%d%d", dev, d.major,
+                d.minor);
+  *out = &d;
+  return LTXFP8_OK;
+}
+
+template <bool kGelu, bool kRequant>
+int gemm_prepare(DeviceInfo* d) {
+  const int idx = (kGelu ? 1 : 0) | (kRequant ? 2 : 0);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (d->gemm_ready[idx]) return LTXFP8_OK;
+  auto kern = fp8_blockwise_gemm_kernel<kGelu, kRequant>;
+  cudaFuncAttributes attr;
+  cudaError_t e = cudaFuncGetAttributes(&attr, kern);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(gemm)");
+  // The warpgroups re-split their registers with setmaxnreg; that only works if
+  // the launch reserves the full per-thread budget the split assumes.
+  if (attr.numRegs < static_cast<int>(kGemmLaunchRegs))
+    return fail(LTXFP8_ERR_CUDA, "gemm kernel compiled with %d registers/thread, register split needs %u",
+                attr.numRegs, kGemmLaunchRegs);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm smem)");
+  d->gemm_ready[idx] = true;
+  return LTXFP8_OK;
+}
+
+template <bool kGelu, bool kRequant>
+int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
+                const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
+  int rc = gemm_prepare<kGelu, kRequant>(d);
+  if (rc) return rc;
+  const int grid = p.total_tiles < d->sms ? p.total_tiles : d->sms;
+  fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return LTXFP8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ltxfp8_version(void) { return (1 << 16) | 0; }
+
+const char* ltxfp8_last_error(void) { return t_last_error.c_str(); }
+
+int ltxfp8_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld, float* sfa,
+                          int64_t sfa_ld, int flags, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "quantize: need K %% 128 == 0, K > 0, M >= 0 (M=%lld K=%lld)", (long long)M, (long long)K);
+  if (flags != LTXFP8_QUANT_TORCH && flags != LTXFP8_QUANT_TRITON) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize: unknown mode %d", flags);
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !q || !sfa) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize: null pointer");
+  if (x_ld < K || q_ld < K || sfa_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize: leading dimension too small");
+  if (!aligned(x, 16) || x_ld % 8 != 0) return fail(LTXFP8_ERR_MISALIGNED, "quantize: x must be 16-byte aligned with x_ld %% 8 == 0");
+  if (!aligned(q, 8) || q_ld % 8 != 0) return fail(LTXFP8_ERR_MISALIGNED, "quantize: q must be 8-byte aligned with q_ld %% 8 == 0");
+  if (!aligned(sfa, 4)) return fail(LTXFP8_ERR_MISALIGNED, "quantize: sfa must be 4-byte aligned");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t KB = K / 128;
+  dim3 grid(static_cast<unsigned>((M + kQuantRowsPerBlock - 1) / kQuantRowsPerBlock),
+            static_cast<unsigned>((KB + kQuantGroupsPerThread - 1) / kQuantGroupsPerThread));
+  if (grid.y > 65535u) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "quantize: K too large");
+  auto s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* qb = static_cast<uint8_t*>(q);
+  if (flags == LTXFP8_QUANT_TRITON)
+    quant_act_1x128_kernel<kQuantTriton><<<grid, 256, 0, s>>>(xb, x_ld, M, KB, qb, q_ld, sfa, sfa_ld);
+  else
+    quant_act_1x128_kernel<kQuantTorch><<<grid, 256, 0, s>>>(xb, x_ld, M, KB, qb, q_ld, sfa, sfa_ld);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_quantize_weight_128x128(const void* w, int dtype, int64_t N, int64_t K, void* q, float* sfb,
+                                   void* stream) {
+  if (N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "quantize_weight: N and K must be positive multiples of 128 (N=%lld K=%lld)", (long long)N, (long long)K);
+  if (dtype < LTXFP8_DTYPE_F32 || dtype > LTXFP8_DTYPE_F16) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize_weight: unknown dtype %d", dtype);
+  if (!w || !q || !sfb) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize_weight: null pointer");
+  if (!aligned(w, 16) || !aligned(q, 16) || !aligned(sfb, 4)) return fail(LTXFP8_ERR_MISALIGNED, "quantize_weight: w and q must be 16-byte aligned");
+  if (N / 128 > 65535) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "quantize_weight: N too large");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
+  quant_weight_128x128_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(w, dtype, K, K / 128,
+                                                                                    static_cast<uint8_t*>(q), sfb);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_weight launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stride, int64_t col_stride, int64_t M,
+                            int64_t K, void* out, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "dequantize: K must be a positive multiple of 128");
+  if (M == 0) return LTXFP8_OK;
+  if (!q || !scales || !out) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "dequantize: null pointer");
+  if (!aligned(q, 16) || !aligned(out, 16) || !aligned(scales, 4)) return fail(LTXFP8_ERR_MISALIGNED, "dequantize: q and out must be 16-byte aligned");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t chunks = M * (K / 16);
+  int64_t blocks = (chunks + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(d->sms) * 8;
+  if (blocks > cap) blocks = cap;
+  dequant_1x128_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(q), scales, row_stride, col_stride, M, K, static_cast<__nv_bfloat16*>(out));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dequantize launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
+                void* stream) {
+  ltxfp8_epilogue none;
+  memset(&none, 0, sizeof(none));
+  const ltxfp8_epilogue& e = ep ? *ep : none;
+  if (M < 1 || N < 128 || K < 128 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gemm: need M >= 1 and N, K positive multiples of 128 (M=%lld N=%lld K=%lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gemm: dimension exceeds int32");
+  if (!A || !sfa || !W || !sfb) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: null operand");
+  if (sfa_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: sfa_ld (%lld) < M (%lld)", (long long)sfa_ld, (long long)M);
+  const bool write_d = !e.skip_d;
+  if (write_d && !D) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: D is null");
+  if (!write_d && !e.requant_q) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: skip_d needs requant_q");
+  if (!aligned(A, 16) || !aligned(W, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: A and W must be 16-byte aligned");
+  if (write_d && !aligned(D, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: D must be 16-byte aligned");
+  if (!aligned(sfa, 4) || !aligned(sfb, 4)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: scales must be 4-byte aligned");
+  if (bias && !aligned(bias, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: bias must be 16-byte aligned");
+  if (e.requant_q) {
+    if (!e.requant_scales) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: requant_scales is null");
+    if (e.requant_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: requant_ld < M");
+    if (!aligned(e.requant_q, 16) || !aligned(e.requant_scales, 4)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: requant outputs misaligned");
+  }
+  const bool lora = e.lora_ax != nullptr;
+  if (lora) {
+    if (!e.lora_b) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: lora_b is null");
+    if (e.lora_r < 16 || e.lora_r > 256 || e.lora_r % 16 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gemm: lora_r must be a multiple of 16 in [16, 256]");
+    if (!aligned(e.lora_ax, 16) || !aligned(e.lora_b, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: LoRA operands must be 16-byte aligned");
+  }
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+
+  CUtensorMap ma, mb, mlx, mlb;
+  rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, K, kBK, kBM);
+  if (rc) return rc;
+  rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, kBN);
+  if (rc) return rc;
+  if (lora) {
+    rc = make_map_2d(&mlx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_ax, e.lora_r, M, e.lora_r * 2, kLoraChunk, kBM);
+    if (rc) return rc;
+    rc = make_map_2d(&mlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_b, e.lora_r, N, e.lora_r * 2, kLoraChunk, kBN);
+    if (rc) return rc;
+  } else {
+    mlx = ma;  // unused
+    mlb = mb;
+  }
+
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.num_kb = static_cast<int>(K / kBK);
+  p.num_lora = lora ? static_cast<int>((e.lora_r + kLoraChunk - 1) / kLoraChunk) : 0;
+  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.n_tiles = static_cast<int>((N + kBN - 1) / kBN);
+  // Group enough M tiles that one group's A slab is ~24 MB: the wave of resident
+  // CTAs then re-reads A and W from L2 rather than HBM.
+  int64_t gm = (24ll << 20) / (static_cast<int64_t>(kBM) * K);
+  if (gm < 1) gm = 1;
+  if (gm > p.m_tiles) gm = p.m_tiles;
+  p.group_m = static_cast<int>(gm);
+  p.total_tiles = p.m_tiles * p.n_tiles;
+  p.sfa = sfa;
+  p.sfa_ld = sfa_ld;
+  p.sfb = sfb;
+  p.bias = bias;
+  p.d = static_cast<__nv_bfloat16*>(D);
+  p.q_out = static_cast<uint8_t*>(e.requant_q);
+  p.s_out = e.requant_scales;
+  p.s_out_ld = e.requant_ld;
+  p.lora_alpha = e.lora_alpha;
+  p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0);
+
+  auto s = static_cast<cudaStream_t>(stream);
+  const bool gelu = e.gelu_tanh != 0, requant = e.requant_q != nullptr;
+  if (gelu && requant) return gemm_launch<true, true>(d, ma, mb, mlx, mlb, p, s);
+  if (gelu) return gemm_launch<true, false>(d, ma, mb, mlx, mlb, p, s);
+  if (requant) return gemm_launch<false, true>(d, ma, mb, mlx, mlb, p, s);
+  return gemm_launch<false, false>(d, ma, mb, mlx, mlb, p, s);
+}
+
+int ltxfp8_lora_a(const void* x, const void* lora_a, void* ax, int64_t M, int64_t K, int64_t r, void* stream) {
+  if (M < 0 || K <= 0 || K % 64 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "lora_a: K must be a positive multiple of 64");
+  if (r < 16 || r > 256 || r % 16 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "lora_a: r must be a multiple of 16 in [16, 256]");
+  if (M == 0) return LTXFP8_OK;
+  if (M > 0x7FFFFFFF || K > 0x7FFFFFFF) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "lora_a: dimension exceeds int32");
+  if (!x || !lora_a || !ax) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "lora_a: null pointer");
+  if (!aligned(x, 16) || !aligned(lora_a, 16) || !aligned(ax, 16)) return fail(LTXFP8_ERR_MISALIGNED, "lora_a: operands must be 16-byte aligned");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  CUtensorMap mx, ma;
+  rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, K * 2, 64, 128);
+  if (rc) return rc;
+  rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lora_a, K, r, K * 2, 64, static_cast<uint32_t>(r));
+  if (rc) return rc;
+  LoraParams p;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.r = static_cast<int>(r);
+  p.num_chunks = static_cast<int>(K / 64);
+  p.stage_bytes = kLoraXBytes + static_cast<uint32_t>(r) * 128u;
+  p.stages = static_cast<int>(kLoraSmemBudget / p.stage_bytes);
+  if (p.stages > 8) p.stages = 8;
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(r)) cols <<= 1;
+  p.tmem_cols = cols;
+  p.ax = static_cast<__nv_bfloat16*>(ax);
+  const uint32_t smem = p.stages * p.stage_bytes + 1024 + 256;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!d->lora_ready) {
+      cudaError_t e = cudaFuncSetAttribute(lora_a_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kLoraSmemBudget + 1024 + 256);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(lora_a smem)");
+      d->lora_ready = true;
+    }
+  }
+  const unsigned grid = static_cast<unsigned>((M + 127) / 128);
+  lora_a_kernel<<<grid, kLoraThreads, smem, static_cast<cudaStream_t>(stream)>>>(mx, ma, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "lora_a launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_device_status(unsigned int* status, int clear, void* stream) {
+  if (!status) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "device_status: null pointer");
+  auto s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_device_status, sizeof(unsigned int), 0,
+                                            cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "device_status read");
+  if (clear) {
+    static const unsigned int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "device_status clear");
+  }
+  return LTXFP8_OK;
+}
+
+}  // extern "C"

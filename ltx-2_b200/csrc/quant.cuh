@@ -1,0 +1,193 @@
+// Quantisation kernels: per-token 1x128 activation quant, 128x128 weight quant,
+// and the 1x128 dequantiser.  All three are HBM-bound streaming kernels.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace ltxfp8 {
+
+// Activation-quant modes.
+enum QuantMode : int {
+  kQuantTorch = 0,   // s = (1/amax)*448 with IEEE roundings, NaN-propagating amax (functional.py:138-144)
+  kQuantTriton = 1,  // s = 448/amax and 1/s via div.full.f32, NaN-ignoring amax (triton_ops.py:13-22)
+};
+
+constexpr int kQuantRowsPerBlock = 16;   // 16 lanes per 128-group, 16 groups per 256-thread block
+constexpr int kQuantGroupsPerThread = 4; // groups in flight per thread (4 x 16 B loads)
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Scale pair for one group from its abs-max.
+template <int kMode>
+__device__ __forceinline__ void group_scale(float amax, float& s, float& inv) {
+  if constexpr (kMode == kQuantTriton) {
+    s = div_full(448.0f, amax);
+    inv = div_full(1.0f, s);
+  } else {
+    s = __fmul_rn(__frcp_rn(amax), 448.0f);
+    inv = __frcp_rn(s);
+  }
+}
+
+// x: bf16 [M, K] (row stride x_ld elements) -> q: e4m3 [M, K] (row stride q_ld),
+// sfa[kb * sfa_ld + m] = 1 / s.  Block = 16 rows x kQuantGroupsPerThread groups;
+// each half-warp owns one row-group of 128 values (8 per lane, one 16 B load).
+// Replaces _block_quant_kernel (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:102-126).
+template <int kMode>
+__global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_ld,
+                                                              int64_t M, int64_t KB, uint8_t* __restrict__ q,
+                                                              int64_t q_ld, float* __restrict__ sfa,
+                                                              int64_t sfa_ld) {
+  const int t = threadIdx.x;
+  const int l16 = t & 15;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kQuantRowsPerBlock + (t >> 4);
+  const int64_t kb0 = static_cast<int64_t>(blockIdx.y) * kQuantGroupsPerThread;
+  const bool row_ok = row < M;
+
+  uint4 v[kQuantGroupsPerThread];
+#pragma unroll
+  for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+    const int64_t kb = kb0 + u;
+    if (row_ok && kb < KB) {
+      v[u] = __ldg(reinterpret_cast<const uint4*>(x + row * x_ld + kb * 128 + l16 * 8));
+    } else {
+      v[u] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+#pragma unroll
+  for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+    const int64_t kb = kb0 + u;
+    float f[8];
+    bf16x8_to_f32(v[u], f);
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = (kMode == kQuantTriton) ? fmaxf(amax, fabsf(f[i])) : fmax_nan(amax, fabsf(f[i]));
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) {
+      const float o = __shfl_xor_sync(0xffffffffu, amax, off, 16);
+      amax = (kMode == kQuantTriton) ? fmaxf(amax, o) : fmax_nan(amax, o);
+    }
+    float s, inv;
+    group_scale<kMode>(amax, s, inv);
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(f[4 * i], s), __fmul_rn(f[4 * i + 1], s));
+      const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(f[4 * i + 2], s), __fmul_rn(f[4 * i + 3], s));
+      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    if (row_ok && kb < KB) {
+      *reinterpret_cast<uint2*>(q + row * q_ld + kb * 128 + l16 * 8) = make_uint2(w[0], w[1]);
+      if (l16 == 0) sfa[kb * sfa_ld + row] = inv;
+    }
+  }
+}
+
+// Weight quant over 128x128 blocks: one block of 256 threads per (kb, nb); each
+// thread owns 64 consecutive values of one row.  s = (1/amax)*448, scale = 1/s
+// (ltx-kernels/src/ltx_kernels/blockwise/functional.py:128-135).
+// in_dtype: 0 = fp32, 1 = bf16, 2 = fp16.
+__global__ void __launch_bounds__(256) quant_weight_128x128_kernel(const void* __restrict__ w, int in_dtype, int64_t K,
+                                                                   int64_t KB, uint8_t* __restrict__ q,
+                                                                   float* __restrict__ sfb) {
+  __shared__ float red[8];
+  const int t = threadIdx.x;
+  const int64_t kb = blockIdx.x, nb = blockIdx.y;
+  const int64_t r = nb * 128 + (t >> 1);
+  const int64_t c0 = kb * 128 + (t & 1) * 64;
+  float f[64];
+  if (in_dtype == 0) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(w) + r * K + c0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 a = __ldg(p + i);
+      f[4 * i] = a.x; f[4 * i + 1] = a.y; f[4 * i + 2] = a.z; f[4 * i + 3] = a.w;
+    }
+  } else if (in_dtype == 1) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(w) + r * K + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float g[8];
+      bf16x8_to_f32(__ldg(p + i), g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[8 * i + j] = g[j];
+    }
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __half*>(w) + r * K + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 a = __ldg(p + i);
+      const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&ww[j]);
+        const float2 g = __half22float2(h);
+        f[8 * i + 2 * j] = g.x;
+        f[8 * i + 2 * j + 1] = g.y;
+      }
+    }
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) amax = fmax_nan(amax, fabsf(f[i]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmax_nan(amax, red[i]);
+  const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
+  uint32_t words[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(f[4 * i], s), __fmul_rn(f[4 * i + 1], s));
+    const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(f[4 * i + 2], s), __fmul_rn(f[4 * i + 3], s));
+    words[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(q + r * K + c0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+  if (t == 0) sfb[nb * KB + kb] = __frcp_rn(s);
+}
+
+// Dequant: out[m, k] = bf16(float(q[m, k]) * scales[m * rs + (k / 128) * cs]).
+// Each thread converts 16 codes (one 16 B load, two 16 B stores).
+// Replaces _blockwise_dequantize_kernel (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:387-411).
+__global__ void __launch_bounds__(256) dequant_1x128_kernel(const uint8_t* __restrict__ q, const float* __restrict__ sc,
+                                                            int64_t rs, int64_t cs, int64_t M, int64_t K,
+                                                            __nv_bfloat16* __restrict__ out) {
+  const int64_t chunks_per_row = K / 16;
+  const int64_t total = M * chunks_per_row;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = c / chunks_per_row;
+    const int64_t k0 = (c - m * chunks_per_row) * 16;
+    const float s = __ldg(sc + m * rs + (k0 / 128) * cs);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(q + m * K + k0));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_fp8x2_storage_t lo = static_cast<__nv_fp8x2_storage_t>(w[i] & 0xFFFFu);
+      const __nv_fp8x2_storage_t hi = static_cast<__nv_fp8x2_storage_t>(w[i] >> 16);
+      const float2 a = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(lo, __NV_E4M3)));
+      const float2 b = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(hi, __NV_E4M3)));
+      o[2 * i] = pack_bf16x2(__fmul_rn(a.x, s), __fmul_rn(a.y, s));
+      o[2 * i + 1] = pack_bf16x2(__fmul_rn(b.x, s), __fmul_rn(b.y, s));
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + m * K + k0);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+}  // namespace ltxfp8

@@ -1,0 +1,100 @@
+"""ctypes binding of the sm_100a C-ABI library (``include/ltxfp8.h``).
+
+The library is loaded lazily on first use.  There is no fallback: if the
+library is missing, or the device is not an sm_100 part, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libltxfp8.so")
+
+# Error codes of include/ltxfp8.h
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_UNSUPPORTED_SHAPE = -2
+ERR_MISALIGNED = -3
+ERR_CUDA = -4
+ERR_DEVICE = -5
+ERR_DEVICE_STATUS = -6
+
+QUANT_TORCH = 0
+QUANT_TRITON = 1
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+DTYPE_F16 = 2
+
+_lock = threading.Lock()
+_lib = None
+
+
+class LtxFp8Error(RuntimeError):
+    """Raised when a C-ABI call returns a non-zero code."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ltxfp8 error {code}: {msg}")
+        self.code = code
+
+
+class Epilogue(ctypes.Structure):
+    _fields_ = [
+        ("gelu_tanh", ctypes.c_int),
+        ("requant_q", ctypes.c_void_p),
+        ("requant_scales", ctypes.c_void_p),
+        ("requant_ld", ctypes.c_int64),
+        ("skip_d", ctypes.c_int),
+        ("lora_ax", ctypes.c_void_p),
+        ("lora_b", ctypes.c_void_p),
+        ("lora_r", ctypes.c_int64),
+        ("lora_alpha", ctypes.c_float),
+    ]
+
+
+# name -> (restype, argtypes); the exported symbols of include/ltxfp8.h
+_vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+SIGNATURES = {
+    "ltxfp8_version": (_i32, []),
+    "ltxfp8_last_error": (ctypes.c_char_p, []),
+    "ltxfp8_quantize_1x128": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i32, _vp]),
+    "ltxfp8_quantize_weight_128x128": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _vp]),
+    "ltxfp8_dequantize_1x128": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "ltxfp8_gemm": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.POINTER(Epilogue), _vp]),
+    "ltxfp8_lora_a": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ltxfp8_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _i32, _vp]),
+}
+
+
+def load(path: str | None = None):
+    """Load (once) and return the ctypes handle of libltxfp8.so."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            p = path or LIB_PATH
+            if not os.path.exists(p):
+                raise ImportError(
+                    f"{p} is missing: build the sm_100a library first "
+                    "(python ltx-2_b200/build.py, or __graft_entry__.build())")
+            L = ctypes.CDLL(p)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        msg = load().ltxfp8_last_error().decode(errors="replace")
+        raise LtxFp8Error(rc, msg)
+
+
+def device_status(stream: int = 0, clear: bool = True) -> int:
+    """Read (and by default clear) the kernels' device status word; 0 = healthy."""
+    st = ctypes.c_uint(0)
+    check(load().ltxfp8_device_status(ctypes.byref(st), 1 if clear else 0, stream))
+    return st.value

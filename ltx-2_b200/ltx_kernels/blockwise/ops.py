@@ -1,0 +1,216 @@
+"""Tensor-level wrappers of the sm_100a C-ABI (include/ltxfp8.h).
+
+These functions take and return torch tensors, allocate outputs with torch's
+caching allocator, and launch on the current CUDA stream.  They never
+synchronise and never fall back to another implementation: non-CUDA inputs,
+unsupported shapes and a missing library raise.
+
+Layout conventions are those of Lightricks/LTX-2's ltx-kernels blockwise path:
+activation scales are MN-major -- element (m, kb) at ``sfa[kb * ld + m]`` --
+exposed as an ``(M, K/128)`` view with strides ``(1, align4(M))``
+(ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:134-135).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _lib as L
+
+
+def align4(n: int) -> int:
+    """get_tma_aligned_size(n, 4) (triton_ops.py:9-11)."""
+    return (n + 3) // 4 * 4
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(name: str, *ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name}: ltx-2_b200 kernels need CUDA (sm_100) tensors, got {t.device}")
+
+
+class _DeviceGuard:
+    """Switch to the tensor's device only when it differs from the current one."""
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if self.idx is not None and self.idx != cur:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def scale_layout(s: torch.Tensor, M: int, KB: int) -> int:
+    """Leading dimension of an activation-scale tensor holding (m, kb) at [kb * ld + m].
+
+    Accepts the reference's two layouts: the ``(M, KB)`` MN-major view returned
+    by blockwise::quantize (stride (1, ld)), and the contiguous ``(KB, M)``
+    tensor returned by blockwise_quantize_torch (functional.py:144)."""
+    if s.dtype != torch.float32:
+        raise RuntimeError(f"activation scales must be float32, got {s.dtype}")
+    if tuple(s.shape) == (M, KB) and (s.stride(0) == 1 or M == 1) and (KB == 1 or s.stride(1) >= M):
+        return s.stride(1) if KB > 1 else max(M, 1)
+    if tuple(s.shape) == (KB, M) and (s.stride(1) == 1 or M == 1) and (KB == 1 or s.stride(0) >= M):
+        return s.stride(0) if KB > 1 else max(M, 1)
+    raise RuntimeError(
+        f"activation scales of shape {tuple(s.shape)} strides {s.stride()} are not an MN-major "
+        f"({M}, {KB}) view or a contiguous ({KB}, {M}) tensor")
+
+
+def empty_act_scales(M: int, KB: int, device) -> torch.Tensor:
+    """An (M, KB) fp32 view with strides (1, align4(M)), as blockwise::quantize returns."""
+    ld = align4(M)
+    return torch.empty_strided((M, KB), (1, ld), dtype=torch.float32, device=device)
+
+
+# ----------------------------------------------------------------------------- quantisers
+def quantize_1x128(x: torch.Tensor, mode: int = L.QUANT_TORCH) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [..., K] -> (e4m3 [M, K], fp32 scales (M, K/128) MN-major view)."""
+    _require_cuda("quantize_1x128", x)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"quantize_1x128 expects bf16 input, got {x.dtype}")
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    s = empty_act_scales(M, K // 128 if K % 128 == 0 else 0, x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_quantize_1x128(x2.data_ptr(), M, K, x2.stride(0), q.data_ptr(), K, s.data_ptr(),
+                                                align4(M), mode, _stream(x)))
+    return q, s
+
+
+def quantize_weight_128x128(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """W [N, K] (fp32/bf16/fp16) -> (e4m3 [N, K], fp32 scales [N/128, K/128])."""
+    _require_cuda("quantize_weight_128x128", w)
+    dt = {torch.float32: L.DTYPE_F32, torch.bfloat16: L.DTYPE_BF16, torch.float16: L.DTYPE_F16}.get(w.dtype)
+    if dt is None:
+        raise RuntimeError(f"quantize_weight_128x128: unsupported dtype {w.dtype}")
+    if w.dim() != 2:
+        raise RuntimeError("quantize_weight_128x128 expects a 2-D weight")
+    w = w.contiguous()
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.float8_e4m3fn, device=w.device)
+    s = torch.empty((N // 128, K // 128), dtype=torch.float32, device=w.device)
+    with _DeviceGuard(w):
+        L.check(L.load().ltxfp8_quantize_weight_128x128(w.data_ptr(), dt, N, K, q.data_ptr(), s.data_ptr(),
+                                                         _stream(w)))
+    return q, s
+
+
+def dequantize_1x128(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """e4m3 [M, K] + scales (M, K/128) with any strides -> bf16 [M, K]."""
+    _require_cuda("dequantize_1x128", q, scales)
+    K = q.shape[-1]
+    q2 = q.reshape(-1, K).contiguous()
+    M = q2.shape[0]
+    if scales.dim() != 2 or scales.shape[0] != M:
+        raise RuntimeError(f"dequantize_1x128: scales shape {tuple(scales.shape)} does not match {M} rows")
+    out = torch.empty((M, K), dtype=torch.bfloat16, device=q.device)
+    with _DeviceGuard(q):
+        L.check(L.load().ltxfp8_dequantize_1x128(q2.data_ptr(), scales.data_ptr(), scales.stride(0),
+                                                  scales.stride(1), M, K, out.data_ptr(), _stream(q)))
+    return out
+
+
+# ----------------------------------------------------------------------------- GEMM
+def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Tensor,
+         bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,
+         gelu: bool = False, requant: bool = False, write_d: bool = True,
+         lora_ax: Optional[torch.Tensor] = None, lora_b: Optional[torch.Tensor] = None,
+         lora_alpha: float = 1.0):
+    """Blockwise FP8 GEMM with fused epilogue.
+
+    Returns D (bf16 [M, N]) when ``requant`` is False, else ``(D or None, q, scales)``
+    where ``q``/``scales`` are the 1x128 quantisation of the (GELU'd) bf16 output in
+    the same layout blockwise::quantize produces."""
+    _require_cuda("gemm", a_q, sfa, w_q, sfb, bias, lora_ax, lora_b)
+    if a_q.dim() != 2 or w_q.dim() != 2:
+        raise RuntimeError("gemm expects 2-D operands")
+    M, K = a_q.shape
+    N, K2 = w_q.shape
+    if K != K2:
+        raise RuntimeError(f"gemm: K mismatch ({K} vs {K2})")
+    if a_q.dtype != torch.float8_e4m3fn or w_q.dtype != torch.float8_e4m3fn:
+        raise RuntimeError("gemm: operands must be float8_e4m3fn")
+    if not a_q.is_contiguous() or not w_q.is_contiguous():
+        raise RuntimeError("gemm: operands must be contiguous (K-major)")
+    KB = K // 128
+    ld = scale_layout(sfa, M, KB)
+    if sfb.dtype != torch.float32 or tuple(sfb.shape) != (N // 128, KB) or not sfb.is_contiguous():
+        raise RuntimeError(f"gemm: weight scales must be contiguous fp32 [{N // 128}, {KB}]")
+    if bias is not None:
+        if bias.dtype != torch.float32 or bias.numel() != N:
+            raise RuntimeError("gemm: bias must be fp32 [N] (the SM89 contract takes float*)")
+        bias = bias.contiguous()
+    if requant and not write_d:
+        d = None
+    else:
+        d = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a_q.device)
+    ep = L.Epilogue()
+    ep.gelu_tanh = 1 if gelu else 0
+    q = s = None
+    if requant:
+        q = torch.empty((M, N), dtype=torch.float8_e4m3fn, device=a_q.device)
+        s = empty_act_scales(M, N // 128, a_q.device)
+        ep.requant_q = q.data_ptr()
+        ep.requant_scales = s.data_ptr()
+        ep.requant_ld = align4(M)
+        ep.skip_d = 0 if write_d else 1
+    if lora_ax is not None:
+        if lora_b is None:
+            raise RuntimeError("gemm: lora_b is required with lora_ax")
+        r = lora_ax.shape[1]
+        if lora_ax.dtype != torch.bfloat16 or lora_b.dtype != torch.bfloat16 or tuple(lora_ax.shape) != (M, r) \
+                or tuple(lora_b.shape) != (N, r):
+            raise RuntimeError("gemm: LoRA operands must be bf16 ax [M, r] and B [N, r]")
+        lora_ax = lora_ax.contiguous()
+        lora_b = lora_b.contiguous()
+        ep.lora_ax = lora_ax.data_ptr()
+        ep.lora_b = lora_b.data_ptr()
+        ep.lora_r = r
+        ep.lora_alpha = float(lora_alpha)
+    with _DeviceGuard(a_q):
+        L.check(L.load().ltxfp8_gemm(a_q.data_ptr(), sfa.data_ptr(), ld, w_q.data_ptr(), sfb.data_ptr(),
+                                     None if bias is None else bias.data_ptr(),
+                                     None if d is None else d.data_ptr(), M, N, K, ep, _stream(a_q)))
+    if requant:
+        return d, q, s
+    return d
+
+
+def lora_a(x: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    """x bf16 [..., K] . A bf16 [r, K]^T -> bf16 [M, r]."""
+    _require_cuda("lora_a", x, a)
+    if x.dtype != torch.bfloat16 or a.dtype != torch.bfloat16:
+        raise RuntimeError("lora_a expects bf16 operands")
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K).contiguous()
+    a = a.contiguous()
+    r = a.shape[0]
+    if a.shape[1] != K:
+        raise RuntimeError("lora_a: K mismatch")
+    M = x2.shape[0]
+    ax = torch.empty((M, r), dtype=torch.bfloat16, device=x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_lora_a(x2.data_ptr(), a.data_ptr(), ax.data_ptr(), M, K, r, _stream(x)))
+    return ax
+
+
+def device_status(clear: bool = True) -> int:
+    """The kernels' bounded-wait status word for the current device (0 = healthy)."""
+    return L.device_status(torch.cuda.current_stream().cuda_stream, clear)

@@ -1,0 +1,236 @@
+/*
+ * CPU oracle for the blockwise-FP8 linear path.  TEST INFRASTRUCTURE ONLY.
+ *
+ * This file restates, in plain C, the arithmetic of Lightricks/LTX-2's
+ * `ltx-kernels` blockwise path so that the CUDA kernels can be checked
+ * against it.  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline leg may load it; the product path never does.
+ *
+ * Every function cites the reference lines it follows (paths are relative
+ * to the reference repository's packages/ directory).
+ *
+ * Conventions
+ *   bf16 values travel as uint16_t bit patterns, e4m3fn codes as uint8_t.
+ *   fp32 -> e4m3fn follows torch's c10 conversion (round to nearest even on
+ *   the e4m3 grid, no saturation: magnitudes above 464 become NaN, 0x7F|sign),
+ *   which is what `tensor.to(torch.float8_e4m3fn)` does in
+ *   ltx-kernels/src/ltx_kernels/blockwise/functional.py:133,143.
+ *   The scale is formed the way torch evaluates `scale_max / amax` for a Python
+ *   scalar numerator: Tensor.__rtruediv__ is `self.reciprocal() * other`, so
+ *   s = RN(RN(1 / amax) * scale_max) -- two IEEE roundings, not one division --
+ *   and the stored scale `1 / s` is RN(1 / s) (functional.py:131,134,142,144).
+ *
+ * Parity pin: the quantisers are checked bit-for-bit against fixtures made by
+ * the reference's own torch functions (tests/golden/make_golden.py).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#if defined(__FLT_EVAL_METHOD__) && __FLT_EVAL_METHOD__ != 0
+#error "oracle needs IEEE single-precision evaluation (FLT_EVAL_METHOD 0)"
+#endif
+
+static inline float f32_from_bits(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t bits_from_f32(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+float orc_bf16_to_f32(uint16_t h) { return f32_from_bits((uint32_t)h << 16); }
+
+/* fp32 -> bf16, round to nearest even; NaN stays a quiet NaN of the same sign. */
+uint16_t orc_f32_to_bf16(float f) {
+    uint32_t u = bits_from_f32(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
+    uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7fffu + lsb;
+    return (uint16_t)(u >> 16);
+}
+
+/* e4m3fn code -> fp32 (exact).  0x7F / 0xFF are NaN; there is no infinity. */
+float orc_e4m3_to_f32(uint8_t c) {
+    uint32_t s = (c >> 7) & 1u, e = (c >> 3) & 0xfu, m = c & 7u;
+    float v;
+    if (e == 15u && m == 7u) return s ? -NAN : NAN;
+    if (e == 0u) v = ldexpf((float)m, -9);                 /* subnormal: m * 2^-9 */
+    else v = ldexpf(1.0f + (float)m / 8.0f, (int)e - 7);   /* normal */
+    return s ? -v : v;
+}
+
+/* fp32 -> e4m3fn code with c10 semantics (round to nearest even, overflow to NaN). */
+uint8_t orc_f32_to_e4m3(float f) {
+    uint32_t u = bits_from_f32(f);
+    uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+    uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return (uint8_t)(sign | 0x7fu);   /* NaN */
+    float x = f32_from_bits(a);
+    /* 464 is the midpoint between 448 (max finite) and 480 (the NaN pattern);
+       ties go to the even code 0x7E, anything above rounds onto the NaN pattern. */
+    if (x > 464.0f) return (uint8_t)(sign | 0x7fu);
+    if (x >= 0.015625f) {                                  /* normal range, >= 2^-6 */
+        int e; float fr = frexpf(x, &e);                    /* x = fr * 2^e, fr in [0.5,1) */
+        /* mantissa in units of 2^(e-1-3): x / 2^(e-4) in [8,16) */
+        float scaled = ldexpf(fr, 4);                       /* in [8,16) exactly */
+        float r = nearbyintf(scaled);                       /* RNE (default rounding mode) */
+        int ee = e - 1 + 7;                                 /* biased exponent */
+        int mm = (int)r - 8;
+        if (mm == 8) { mm = 0; ee += 1; }
+        if (ee > 15) return (uint8_t)(sign | 0x7fu);
+        return (uint8_t)(sign | (uint8_t)(ee << 3) | (uint8_t)mm);
+    }
+    /* subnormal range: multiples of 2^-9 */
+    float r = nearbyintf(ldexpf(x, 9));
+    int mm = (int)r;
+    if (mm >= 8) return (uint8_t)(sign | (1u << 3));       /* rounds up to 2^-6 */
+    return (uint8_t)(sign | (uint8_t)mm);
+}
+
+/* abs-max with NaN propagation, as torch's `abs().max()` reduction does. */
+static inline float amax_nan(float a, float b) {
+    if (isnan(a) || isnan(b)) return NAN;
+    return a > b ? a : b;
+}
+
+/*
+ * Activation quantisation, 1x128 groups per token.
+ * Follows blockwise_quantize_torch (ltx-kernels/src/ltx_kernels/blockwise/functional.py:138-144)
+ * and the Triton _quantize/_block_quant_kernel (triton_ops.py:13-22,102-126):
+ *   s = (1 / amax(|x|)) * 448 (torch's reciprocal-then-multiply, see the header);
+ *   q = e4m3(float(x) * s); stored scale = 1 / s.
+ * x: bf16 [M, K] with row stride x_ld; q: [M, K] row stride q_ld;
+ * sfa: MN-major, element (m, kb) at sfa[kb * sfa_ld + m] (triton_ops.py:134-135,147-148).
+ * scale_max is 448 for FP8 (functional.py:21).
+ */
+void orc_quant_act_1x128(const uint16_t* x, int64_t M, int64_t K, int64_t x_ld,
+                         uint8_t* q, int64_t q_ld, float* sfa, int64_t sfa_ld,
+                         float scale_max) {
+    int64_t KB = K / 128;
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t kb = 0; kb < KB; ++kb) {
+            const uint16_t* g = x + m * x_ld + kb * 128;
+            float amax = 0.0f;
+            for (int i = 0; i < 128; ++i) amax = amax_nan(amax, fabsf(orc_bf16_to_f32(g[i])));
+            volatile float r = 1.0f / amax;
+            volatile float s = r * scale_max;
+            for (int i = 0; i < 128; ++i) {
+                volatile float v = orc_bf16_to_f32(g[i]) * s;
+                q[m * q_ld + kb * 128 + i] = orc_f32_to_e4m3(v);
+            }
+            volatile float inv = 1.0f / s;
+            sfa[kb * sfa_ld + m] = inv;
+        }
+    }
+}
+
+/*
+ * Weight quantisation, 128x128 blocks.
+ * Follows blockwise_quantize_weights (functional.py:128-135):
+ *   s = (1 / amax) * 448 over the 128x128 block; q = e4m3(float(w) * s); scale = 1 / s,
+ *   scales stored row-major [N/128, K/128].
+ * w_dtype: 0 = fp32, 1 = bf16 (bit patterns).
+ */
+void orc_quant_weight_128x128(const void* w, int w_dtype, int64_t N, int64_t K,
+                              uint8_t* q, float* sfb, float scale_max) {
+    int64_t NB = N / 128, KB = K / 128;
+    const float* wf = (const float*)w;
+    const uint16_t* wh = (const uint16_t*)w;
+#define WVAL(r, c) (w_dtype == 0 ? wf[(r) * K + (c)] : orc_bf16_to_f32(wh[(r) * K + (c)]))
+    for (int64_t nb = 0; nb < NB; ++nb) {
+        for (int64_t kb = 0; kb < KB; ++kb) {
+            float amax = 0.0f;
+            for (int64_t r = nb * 128; r < nb * 128 + 128; ++r)
+                for (int64_t c = kb * 128; c < kb * 128 + 128; ++c)
+                    amax = amax_nan(amax, fabsf(WVAL(r, c)));
+            volatile float rcp = 1.0f / amax;
+            volatile float s = rcp * scale_max;
+            for (int64_t r = nb * 128; r < nb * 128 + 128; ++r)
+                for (int64_t c = kb * 128; c < kb * 128 + 128; ++c) {
+                    volatile float v = WVAL(r, c) * s;
+                    q[r * K + c] = orc_f32_to_e4m3(v);
+                }
+            volatile float inv = 1.0f / s;
+            sfb[nb * KB + kb] = inv;
+        }
+    }
+#undef WVAL
+}
+
+/*
+ * Dequantisation to bf16: out = bf16(float(q) * scale[m, k/128]).
+ * Follows _blockwise_dequantize_kernel (triton_ops.py:387-411): the scale of
+ * (row, block) is read at scales[row * row_stride + block * col_stride].
+ */
+void orc_dequant_1x128(const uint8_t* q, const float* scales, int64_t row_stride,
+                       int64_t col_stride, int64_t M, int64_t K, uint16_t* out) {
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t k = 0; k < K; ++k) {
+            float s = scales[m * row_stride + (k / 128) * col_stride];
+            volatile float v = orc_e4m3_to_f32(q[m * K + k]) * s;
+            out[m * K + k] = orc_f32_to_bf16(v);
+        }
+}
+
+/*
+ * Blockwise GEMM in the reference kernel's promotion order
+ * (ltx-kernels/csrc/blockwise/kernels/geforce/gemm.cu:150-222):
+ *   for each 128-wide K block: p = sum_k e4m3(A[m,k]) * e4m3(W[n,k])  (fp32)
+ *                              D += (sfa[m,kb] * sfb[n/128,kb]) * p
+ *   D += bias[n];  out = bf16(D)
+ * A [M,K] codes, W [N,K] codes, sfa at sfa[kb*sfa_ld + m], sfb [N/128, K/128].
+ * bias may be NULL.  Writes fp32 D (before the bf16 cast) to out_f32 if given
+ * and the bf16 result to out_bf16 if given.
+ */
+void orc_gemm_promoted(const uint8_t* A, const float* sfa, int64_t sfa_ld,
+                       const uint8_t* W, const float* sfb, const float* bias,
+                       int64_t M, int64_t N, int64_t K,
+                       float* out_f32, uint16_t* out_bf16) {
+    int64_t KB = K / 128;
+    float lut[256];
+    for (int i = 0; i < 256; ++i) lut[i] = orc_e4m3_to_f32((uint8_t)i);
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t n = 0; n < N; ++n) {
+            float d = 0.0f;
+            for (int64_t kb = 0; kb < KB; ++kb) {
+                float p = 0.0f;
+                const uint8_t* a = A + m * K + kb * 128;
+                const uint8_t* w = W + n * K + kb * 128;
+                for (int i = 0; i < 128; ++i) p = fmaf(lut[a[i]], lut[w[i]], p);
+                float s = sfa[kb * sfa_ld + m] * sfb[(n / 128) * KB + kb];
+                d = fmaf(s, p, d);
+            }
+            if (bias) d += bias[n];
+            if (out_f32) out_f32[m * N + n] = d;
+            if (out_bf16) out_bf16[m * N + n] = orc_f32_to_bf16(d);
+        }
+    }
+}
+
+/*
+ * GELU, tanh approximation, on bf16 values, result rounded to bf16.
+ * The reference applies torch.nn.functional.gelu(x, approximate="tanh") to the
+ * GEMM's bf16 output (ltx-core/src/ltx_core/model/transformer/gelu_approx.py:10):
+ *   0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3))) in fp32, cast to bf16.
+ */
+uint16_t orc_gelu_tanh_bf16(uint16_t xh) {
+    float x = orc_bf16_to_f32(xh);
+    const float kBeta = 0.7978845608028654f;   /* sqrt(2/pi) */
+    const float kKappa = 0.044715f;
+    float x3 = x * x * x;
+    float inner = kBeta * fmaf(kKappa, x3, x);
+    float y = 0.5f * x * (1.0f + tanhf(inner));
+    return orc_f32_to_bf16(y);
+}
+
+void orc_gelu_tanh_bf16_array(const uint16_t* x, int64_t n, uint16_t* y) {
+    for (int64_t i = 0; i < n; ++i) y[i] = orc_gelu_tanh_bf16(x[i]);
+}
+
+void orc_e4m3_to_f32_array(const uint8_t* c, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = orc_e4m3_to_f32(c[i]);
+}
+
+void orc_f32_to_e4m3_array(const float* f, int64_t n, uint8_t* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = orc_f32_to_e4m3(f[i]);
+}
+
+void orc_f32_to_bf16_array(const float* f, int64_t n, uint16_t* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = orc_f32_to_bf16(f[i]);
+}

@@ -1,0 +1,236 @@
+"""CPU oracle for the blockwise-FP8 linear path.  TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+may import this module; the product path (``ltx-2_b200/``) never does.
+
+Two layers:
+
+* ``liboracle`` -- ``ltxfp8_oracle.c`` compiled with gcc: the bit-exact
+  restatements of the reference's quantisers, dequantiser and the SM89 GEMM's
+  per-128-K promotion order.  Each C function cites the reference lines it
+  follows.
+* numpy helpers -- the reference's CPU GEMM path (dequantise both operands, fp32
+  matmul, add fp32 bias, cast to bf16), as described for the CPU baseline of
+  ``blockwise_quantize_torch`` + ``blockwise_quantize_weights``
+  (ltx-kernels/src/ltx_kernels/blockwise/functional.py:128-144), plus the exact
+  LoRA math ``dequant(W) x + alpha * B (A x)`` for the runtime-LoRA extension.
+
+bf16 tensors are carried as ``np.uint16`` bit patterns, e4m3 codes as ``np.uint8``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SRC = os.path.join(_HERE, "ltxfp8_oracle.c")
+_BUILD = os.path.join(_HERE, "_build")
+_LIB_PATH = os.path.join(_BUILD, "liboracle.so")
+
+FP8_SCALE_MAX = 448.0
+
+
+def build(force: bool = False) -> str:
+    """Compile the C oracle with gcc (IEEE single precision, no FMA contraction)."""
+    os.makedirs(_BUILD, exist_ok=True)
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(_SRC):
+        cmd = ["gcc", "-O2", "-fPIC", "-shared", "-std=c11", "-ffp-contract=off", "-fno-fast-math",
+               "-o", _LIB_PATH, _SRC, "-lm"]
+        subprocess.check_call(cmd)
+    return _LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        vp, i64, f32, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int
+        L.orc_quant_act_1x128.argtypes = [vp, i64, i64, i64, vp, i64, vp, i64, f32]
+        L.orc_quant_weight_128x128.argtypes = [vp, i32, i64, i64, vp, vp, f32]
+        L.orc_dequant_1x128.argtypes = [vp, vp, i64, i64, i64, i64, vp]
+        L.orc_gemm_promoted.argtypes = [vp, vp, i64, vp, vp, vp, i64, i64, i64, vp, vp]
+        L.orc_gelu_tanh_bf16_array.argtypes = [vp, i64, vp]
+        L.orc_e4m3_to_f32_array.argtypes = [vp, i64, vp]
+        L.orc_f32_to_e4m3_array.argtypes = [vp, i64, vp]
+        L.orc_f32_to_bf16_array.argtypes = [vp, i64, vp]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def align4(n: int) -> int:
+    """get_tma_aligned_size(n, 4) of triton_ops.py:9-11."""
+    return (n + 3) // 4 * 4
+
+
+# ----------------------------------------------------------------------------- conversions
+def bf16_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f: np.ndarray) -> np.ndarray:
+    f = np.ascontiguousarray(f, dtype=np.float32)
+    out = np.empty(f.shape, np.uint16)
+    lib().orc_f32_to_bf16_array(_p(f), f.size, _p(out))
+    return out
+
+
+_E4M3_LUT = None
+
+
+def e4m3_to_f32(c: np.ndarray) -> np.ndarray:
+    global _E4M3_LUT
+    if _E4M3_LUT is None:
+        codes = np.arange(256, dtype=np.uint8)
+        _E4M3_LUT = np.empty(256, np.float32)
+        lib().orc_e4m3_to_f32_array(_p(codes), 256, _p(_E4M3_LUT))
+    return _E4M3_LUT[np.asarray(c, dtype=np.uint8)]
+
+
+def f32_to_e4m3(f: np.ndarray) -> np.ndarray:
+    f = np.ascontiguousarray(f, dtype=np.float32)
+    out = np.empty(f.shape, np.uint8)
+    lib().orc_f32_to_e4m3_array(_p(f), f.size, _p(out))
+    return out
+
+
+# ----------------------------------------------------------------------------- quantisers
+def quant_act_1x128(x_bf16: np.ndarray, sfa_ld: int | None = None):
+    """Activation quant, 1x128 groups (functional.py:138-144, triton_ops.py:102-151).
+
+    Returns (codes uint8 [M,K], scale buffer float32 [K/128, sfa_ld]); the scale of
+    (m, kb) sits at buffer[kb, m], i.e. the MN-major layout of triton_ops.py:134-135.
+    Entries m >= M of the buffer are left NaN (the reference leaves them unset).
+    """
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    M, K = x.shape
+    assert K % 128 == 0
+    ld = align4(M) if sfa_ld is None else sfa_ld
+    q = np.empty((M, K), np.uint8)
+    sfa = np.full((K // 128, ld), np.nan, np.float32)
+    lib().orc_quant_act_1x128(_p(x), M, K, K, _p(q), K, _p(sfa), ld, FP8_SCALE_MAX)
+    return q, sfa
+
+
+def quant_weight_128x128(w: np.ndarray):
+    """Weight quant, 128x128 blocks (functional.py:128-135).  w: float32 or bf16 bits."""
+    if w.dtype == np.uint16:
+        dt = 1
+    else:
+        w = w.astype(np.float32)
+        dt = 0
+    w = np.ascontiguousarray(w)
+    N, K = w.shape
+    assert N % 128 == 0 and K % 128 == 0
+    q = np.empty((N, K), np.uint8)
+    s = np.empty((N // 128, K // 128), np.float32)
+    lib().orc_quant_weight_128x128(_p(w), dt, N, K, _p(q), _p(s), FP8_SCALE_MAX)
+    return q, s
+
+
+def dequant_1x128(q: np.ndarray, scales: np.ndarray, row_stride: int, col_stride: int) -> np.ndarray:
+    """bf16 dequant with strided scales (triton_ops.py:387-433)."""
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    M, K = q.shape
+    sc = np.ascontiguousarray(scales, dtype=np.float32)
+    out = np.empty((M, K), np.uint16)
+    lib().orc_dequant_1x128(_p(q), _p(sc), row_stride, col_stride, M, K, _p(out))
+    return out
+
+
+def gelu_tanh_bf16(x_bf16: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    y = np.empty_like(x)
+    lib().orc_gelu_tanh_bf16_array(_p(x), x.size, _p(y))
+    return y
+
+
+# ----------------------------------------------------------------------------- GEMM oracles
+def gemm_promoted(A, sfa, sfa_ld, W, sfb, bias, M, N, K):
+    """The SM89 kernel's promotion order in scalar C (gemm.cu:150-222).  Small sizes only.
+
+    Returns (fp32 result before the bf16 cast, bf16 result)."""
+    A = np.ascontiguousarray(A, np.uint8)
+    W = np.ascontiguousarray(W, np.uint8)
+    sfa = np.ascontiguousarray(sfa, np.float32)
+    sfb = np.ascontiguousarray(sfb, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    f = np.empty((M, N), np.float32)
+    h = np.empty((M, N), np.uint16)
+    lib().orc_gemm_promoted(_p(A), _p(sfa), sfa_ld, _p(W), _p(sfb), _p(b), M, N, K, _p(f), _p(h))
+    return f, h
+
+
+def dequant_act_f32(q: np.ndarray, sfa: np.ndarray, rows: np.ndarray | None = None) -> np.ndarray:
+    """fp32 dequant of activation codes with an MN-major scale buffer [K/128, ld]."""
+    M, K = q.shape
+    idx = np.arange(M) if rows is None else rows
+    s = sfa[:, idx].T                                   # [len(idx), K/128]
+    return e4m3_to_f32(q[idx]) * np.repeat(s, 128, axis=1)
+
+
+def dequant_weight_f32(wq: np.ndarray, sfb: np.ndarray) -> np.ndarray:
+    s = np.repeat(np.repeat(sfb, 128, axis=0), 128, axis=1)
+    return e4m3_to_f32(wq) * s
+
+
+def gemm_dequant_f32(aq, sfa, wq, sfb, bias=None, rows=None, w_deq=None) -> np.ndarray:
+    """The reference's CPU path: dequantise, fp32 matmul, add fp32 bias (fp32 result).
+
+    ``rows`` restricts the check to a subset of output rows (for full-size shapes).
+    ``w_deq`` may pass a precomputed dequantised weight."""
+    a = dequant_act_f32(aq, sfa, rows)
+    w = dequant_weight_f32(wq, sfb) if w_deq is None else w_deq
+    d = a @ w.T
+    if bias is not None:
+        d = d + bias.astype(np.float32)[None, :]
+    return d.astype(np.float32)
+
+
+def lora_exact_f32(x_bf16_rows: np.ndarray, lora_a_bf16: np.ndarray, lora_b_bf16: np.ndarray,
+                   alpha: float) -> np.ndarray:
+    """alpha * B (A x) in fp32 from bf16 operands (the runtime-LoRA term)."""
+    x = bf16_to_f32(x_bf16_rows)
+    a = bf16_to_f32(lora_a_bf16)
+    b = bf16_to_f32(lora_b_bf16)
+    return (alpha * ((x @ a.T) @ b.T)).astype(np.float32)
+
+
+# ----------------------------------------------------------------------------- metrics
+def error_metrics(out: np.ndarray, ref: np.ndarray) -> dict:
+    """Relative Frobenius error, max-abs error and max-abs error normalised by max|ref|."""
+    o = out.astype(np.float64)
+    r = ref.astype(np.float64)
+    diff = o - r
+    fro = float(np.linalg.norm(diff) / max(np.linalg.norm(r), 1e-30))
+    mx = float(np.max(np.abs(diff))) if diff.size else 0.0
+    scale = float(np.max(np.abs(r))) if r.size else 1.0
+    return {"rel_fro": fro, "max_abs": mx, "max_abs_norm": mx / max(scale, 1e-30)}
+
+
+def codes_equal(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Bitwise equality of e4m3 codes where both NaN encodings (0x7F, 0xFF) count as equal.
+
+    A 0 * inf product yields the host FPU's default NaN (negative on x86, positive on
+    the GPU); the sign of that NaN carries no information."""
+    a = np.asarray(a, np.uint8)
+    b = np.asarray(b, np.uint8)
+    nan_a = (a & 0x7F) == 0x7F
+    nan_b = (b & 0x7F) == 0x7F
+    return (a == b) | (nan_a & nan_b)
+
+
+def scales_equal(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Bitwise fp32 equality, NaN == NaN."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    return (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
