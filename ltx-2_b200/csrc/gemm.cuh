@@ -44,8 +44,8 @@ constexpr uint32_t kGemmSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256
 
 // Register split between the producer/MMA warpgroup and the two epilogue
 // warpgroups; the launch must provide kGemmThreads * kGemmLaunchRegs.
-constexpr uint32_t kRegsCtrl = 56;
-constexpr uint32_t kRegsEpi = 224;
+constexpr uint32_t kRegsCtrl = 40;
+constexpr uint32_t kRegsEpi = 232;
 constexpr uint32_t kGemmLaunchRegs = 168;
 static_assert(128 * kRegsCtrl + 256 * kRegsEpi <= kGemmThreads * kGemmLaunchRegs, "register split exceeds launch");
 
@@ -91,6 +91,42 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, const GemmParams& p, 
   const int r = tile - g * per_group;
   mt = first_m + r % gm;
   nt = r / gm;
+}
+
+constexpr int kScalePrefetch = 4;
+
+// Fold one K block's raw partial sums (TMEM buffer `it & 1`) into the fp32
+// accumulators of this thread's row: acc += scale * partial, 128 columns as 64
+// packed f32x2 FMAs.  Releases the TMEM buffer as soon as it has been read.
+__device__ __forceinline__ bool promote_kblock(uint64_t* tfull, uint64_t* tempty, uint32_t tmem_base, int sp,
+                                               int half, uint32_t it, float scale, int lane, float2 (&acc)[64]) {
+  const uint32_t buf = it & 1u, bph = (it >> 1) & 1u;
+  // Warp-uniform outcome: the TMEM loads below are .sync.aligned.
+  if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], bph, kStEpiTmemFull))) return false;
+  tc_fence_after_sync();
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + buf * kBN + half * 128;
+  const float2 s2 = make_float2(scale, scale);
+  uint32_t r0[32], r1[32];
+  tmem_ld_32x32b_x32(taddr + 0, r0);
+  tmem_ld_32x32b_x32(taddr + 32, r1);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    acc[j] = __ffma2_rn(s2, make_float2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1])), acc[j]);
+    acc[16 + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1])), acc[16 + j]);
+  }
+  tmem_ld_32x32b_x32(taddr + 64, r0);
+  tmem_ld_32x32b_x32(taddr + 96, r1);
+  tmem_wait_ld();
+  tc_fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    acc[32 + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1])), acc[32 + j]);
+    acc[48 + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1])), acc[48 + j]);
+  }
+  return true;
 }
 
 template <bool kGelu, bool kRequant>
@@ -234,60 +270,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const float* sfa_row = p.sfa + row;
       const float* sfb_blk = p.sfb + static_cast<int64_t>(nb) * p.num_kb;
 
-      float acc[128];
+      float2 acc[64];  // column pairs (2j, 2j+1) of this thread's row
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
 
-      // Scales are prefetched two K blocks ahead of their use.
-      float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-      if (row_ok) {
-        a0 = __ldg(sfa_row);
-        if (p.num_kb > 1) a1 = __ldg(sfa_row + p.sfa_ld);
-      }
-      if (col_ok) {
-        b0 = __ldg(sfb_blk);
-        if (p.num_kb > 1) b1 = __ldg(sfb_blk + 1);
-      }
-      for (int kb = 0; kb < num_blocks; ++kb, ++it) {
-        float a2 = 0.f, b2 = 0.f;
-        if (kb + 2 < p.num_kb) {
-          if (row_ok) a2 = __ldg(sfa_row + static_cast<int64_t>(kb + 2) * p.sfa_ld);
-          if (col_ok) b2 = __ldg(sfb_blk + kb + 2);
-        }
-        const float scale = kb < p.num_kb ? a0 * b0 : p.lora_alpha;
-        const uint32_t buf = it & 1u, bph = (it >> 1) & 1u;
-        // Warp-uniform outcome: the TMEM loads below are .sync.aligned.
-        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], bph, kStEpiTmemFull))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after_sync();
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + buf * kBN + half * 128;
-        uint32_t r0[32], r1[32];
-        tmem_ld_32x32b_x32(taddr + 0, r0);
-        tmem_ld_32x32b_x32(taddr + 32, r1);
-        tmem_wait_ld();
+      // Scales of K block kb are loaded kScalePrefetch blocks before their use.
+      // The loop body is unrolled kScalePrefetch times so every prefetch lives
+      // in its own register until consumed (no register rotation that would
+      // stall on a load still in flight).
+      float sa[kScalePrefetch], sb[kScalePrefetch];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          acc[j] = fmaf(scale, __uint_as_float(r0[j]), acc[j]);
-          acc[32 + j] = fmaf(scale, __uint_as_float(r1[j]), acc[32 + j]);
-        }
-        tmem_ld_32x32b_x32(taddr + 64, r0);
-        tmem_ld_32x32b_x32(taddr + 96, r1);
-        tmem_wait_ld();
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+      for (int j = 0; j < kScalePrefetch; ++j) {
+        sa[j] = (row_ok && j < p.num_kb) ? __ldg(sfa_row + static_cast<int64_t>(j) * p.sfa_ld) : 0.f;
+        sb[j] = (col_ok && j < p.num_kb) ? __ldg(sfb_blk + j) : 0.f;
+      }
+      for (int kb0 = 0; kb0 < num_blocks && ok; kb0 += kScalePrefetch) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          acc[64 + j] = fmaf(scale, __uint_as_float(r0[j]), acc[64 + j]);
-          acc[96 + j] = fmaf(scale, __uint_as_float(r1[j]), acc[96 + j]);
+        for (int j = 0; j < kScalePrefetch; ++j) {
+          const int kb = kb0 + j;
+          if (kb < num_blocks && ok) {
+            const float scale = kb < p.num_kb ? sa[j] * sb[j] : p.lora_alpha;
+            const int kn = kb + kScalePrefetch;
+            sa[j] = (row_ok && kn < p.num_kb) ? __ldg(sfa_row + static_cast<int64_t>(kn) * p.sfa_ld) : 0.f;
+            sb[j] = (col_ok && kn < p.num_kb) ? __ldg(sfb_blk + kn) : 0.f;
+            ok = promote_kblock(tfull, tempty, tmem_base, sp, half, it, scale, lane, acc);
+            ++it;
+          }
         }
-        a0 = a1; a1 = a2;
-        b0 = b1; b1 = b2;
       }
       if (!ok) break;
       if (!(row_ok && col_ok)) continue;
+      float* accf = reinterpret_cast<float*>(acc);
 
       // ------------------------------------------------ bias (+ GELU) in fp32, bf16 rounding
       const bool has_bias = (p.flags & kGemmBias) != 0;
@@ -296,19 +309,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c = 0; c < 128; c += 4) {
         float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
         if (has_bias) bv = __ldg(bias4 + c / 4);
-        acc[c] += bv.x;
-        acc[c + 1] += bv.y;
-        acc[c + 2] += bv.z;
-        acc[c + 3] += bv.w;
+        accf[c] += bv.x;
+        accf[c + 1] += bv.y;
+        accf[c + 2] += bv.z;
+        accf[c + 3] += bv.w;
       }
       if constexpr (kGelu || kRequant) {
         // The reference materialises bf16(acc + bias), applies GELU on that bf16
         // tensor (result rounded to bf16) and quantises those bf16 values.
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
-          float y = bf16_round(acc[c]);
+          float y = bf16_round(accf[c]);
           if constexpr (kGelu) y = bf16_round(gelu_tanh_f32(y));
-          acc[c] = y;
+          accf[c] = y;
         }
       }
       const int64_t out_off = static_cast<int64_t>(row) * p.N + col0;
@@ -316,15 +329,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint4* dst = reinterpret_cast<uint4*>(p.d + out_off);
 #pragma unroll
         for (int c = 0; c < 128; c += 8) {
-          dst[c / 8] = make_uint4(pack_bf16x2(acc[c], acc[c + 1]), pack_bf16x2(acc[c + 2], acc[c + 3]),
-                                  pack_bf16x2(acc[c + 4], acc[c + 5]), pack_bf16x2(acc[c + 6], acc[c + 7]));
+          dst[c / 8] = make_uint4(pack_bf16x2(accf[c], accf[c + 1]), pack_bf16x2(accf[c + 2], accf[c + 3]),
+                                  pack_bf16x2(accf[c + 4], accf[c + 5]), pack_bf16x2(accf[c + 6], accf[c + 7]));
         }
       }
       if constexpr (kRequant) {
         // One thread owns the whole 1x128 group of its row: no cross-thread reduction.
         float amax = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 128; ++c) amax = fmax_nan(amax, fabsf(acc[c]));
+        for (int c = 0; c < 128; ++c) amax = fmax_nan(amax, fabsf(accf[c]));
         const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
         uint4* qdst = reinterpret_cast<uint4*>(p.q_out + out_off);
 #pragma unroll
@@ -332,8 +345,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(acc[c + 4 * i], s), __fmul_rn(acc[c + 4 * i + 1], s));
-            const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(acc[c + 4 * i + 2], s), __fmul_rn(acc[c + 4 * i + 3], s));
+            const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(accf[c + 4 * i], s), __fmul_rn(accf[c + 4 * i + 1], s));
+            const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(accf[c + 4 * i + 2], s), __fmul_rn(accf[c + 4 * i + 3], s));
             w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
           }
           qdst[c / 16] = make_uint4(w[0], w[1], w[2], w[3]);
