@@ -109,6 +109,14 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
                 void* stream);
 
 /*
+ * Select the GEMM kernel: 0 = default (the one-CTA kernel), 1 = the one-CTA
+ * kernel (128 x 256 tiles per SM), 2 = the CTA-pair kernel (256 x 256 tiles
+ * over two SMs of a cluster, tcgen05 cta_group::2).  Process-wide; meant for tests and tuning.  No reference
+ * counterpart (the reference has one kernel per architecture, linear.py:25-45).
+ */
+int ltxfp8_gemm_set_variant(int variant);
+
+/*
  * LoRA down projection: ax bf16 [M, r] = x bf16 [M, K] . lora_a bf16 [r, K]^T (fp32 accumulation).
  * K % 64 == 0, r % 16 == 0, 16 <= r <= 256.  No reference counterpart: the
  * reference merges LoRA into the weights at load time

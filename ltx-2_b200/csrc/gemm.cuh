@@ -339,14 +339,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) amax = fmax_nan(amax, fabsf(accf[c]));
         const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
+        const bool in_range = isfinite(s);  // then no product exceeds 448: plain hardware conversion
         uint4* qdst = reinterpret_cast<uint4*>(p.q_out + out_off);
 #pragma unroll
         for (int c = 0; c < 128; c += 16) {
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(accf[c + 4 * i], s), __fmul_rn(accf[c + 4 * i + 1], s));
-            const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(accf[c + 4 * i + 2], s), __fmul_rn(accf[c + 4 * i + 3], s));
+            const float v0 = __fmul_rn(accf[c + 4 * i], s), v1 = __fmul_rn(accf[c + 4 * i + 1], s);
+            const float v2 = __fmul_rn(accf[c + 4 * i + 2], s), v3 = __fmul_rn(accf[c + 4 * i + 3], s);
+            const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+            const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
             w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
           }
           qdst[c / 16] = make_uint4(w[0], w[1], w[2], w[3]);

@@ -9,10 +9,12 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
 #include "gemm.cuh"
+#include "gemm_pair.cuh"
 #include "lora.cuh"
 #include "ptx.cuh"
 #include "quant.cuh"
@@ -75,8 +77,13 @@ struct DeviceInfo {
   int sms = 0;
   int major = 0, minor = 0;
   bool gemm_ready[4] = {false, false, false, false};
+  bool pair_ready[4] = {false, false, false, false};
+  int pair_clusters = 0;  // co-resident 2-CTA clusters of the pair kernel
   bool lora_ready = false;
 };
+
+// 0 = choose by shape, 1 = one-CTA kernel, 2 = CTA-pair kernel.
+std::atomic<int> g_gemm_variant{0};
 
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
@@ -130,6 +137,54 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
   fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return LTXFP8_OK;
+}
+
+
+template <bool kGelu, bool kRequant>
+int gemm_pair_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
+                     const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
+  auto kern = pair::fp8_blockwise_gemm_pair_kernel<kGelu, kRequant>;
+  const int idx = (kGelu ? 1 : 0) | (kRequant ? 2 : 0);
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(pair::kThreads);
+  cfg.dynamicSmemBytes = pair::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!d->pair_ready[idx]) {
+      cudaFuncAttributes fa;
+      cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(gemm pair)");
+      if (fa.numRegs < static_cast<int>(pair::kLaunchRegs))
+        return fail(LTXFP8_ERR_CUDA, "pair gemm kernel compiled with %d registers/thread, register split needs %u",
+                    fa.numRegs, pair::kLaunchRegs);
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair smem)");
+      // A persistent grid must fit in one wave: launch exactly as many clusters as can be resident.
+      cfg.gridDim = dim3(2 * (d->sms / 2));
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters(gemm pair)");
+      if (n < 1) return fail(LTXFP8_ERR_CUDA, "no 2-CTA cluster of the pair gemm fits on this device");
+      d->pair_clusters = n;
+      d->pair_ready[idx] = true;
+    }
+  }
+  const int clusters = p.total_tiles < d->pair_clusters ? p.total_tiles : d->pair_clusters;
+  cfg.gridDim = dim3(2 * clusters);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, lx, lb, p);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   return LTXFP8_OK;
 }
 
@@ -243,15 +298,25 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   int rc = device_info(&d);
   if (rc) return rc;
 
+  // Default: the one-CTA kernel.  The CTA-pair kernel (256-row tiles over two
+  // SMs) is selected explicitly; it halves the W bytes each SM streams but is
+  // not yet faster on the FFN shapes.
+  const int variant = g_gemm_variant.load();
+  const bool use_pair = variant == 2;
+  const int tile_m = use_pair ? pair::kTileM : kBM;
+  const int tile_n = use_pair ? pair::kTileN : kBN;
+  const uint32_t w_rows_per_load = use_pair ? pair::kRowsPerCta : kBN;  // N rows each CTA loads
+
   CUtensorMap ma, mb, mlx, mlb;
   rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, K, kBK, kBM);
   if (rc) return rc;
-  rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, kBN);
+  rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, w_rows_per_load);
   if (rc) return rc;
   if (lora) {
     rc = make_map_2d(&mlx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_ax, e.lora_r, M, e.lora_r * 2, kLoraChunk, kBM);
     if (rc) return rc;
-    rc = make_map_2d(&mlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_b, e.lora_r, N, e.lora_r * 2, kLoraChunk, kBN);
+    rc = make_map_2d(&mlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_b, e.lora_r, N, e.lora_r * 2, kLoraChunk,
+                     w_rows_per_load);
     if (rc) return rc;
   } else {
     mlx = ma;  // unused
@@ -265,11 +330,11 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   p.K = static_cast<int>(K);
   p.num_kb = static_cast<int>(K / kBK);
   p.num_lora = lora ? static_cast<int>((e.lora_r + kLoraChunk - 1) / kLoraChunk) : 0;
-  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
-  p.n_tiles = static_cast<int>((N + kBN - 1) / kBN);
+  p.m_tiles = static_cast<int>((M + tile_m - 1) / tile_m);
+  p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   // Group enough M tiles that one group's A slab is ~24 MB: the wave of resident
   // CTAs then re-reads A and W from L2 rather than HBM.
-  int64_t gm = (24ll << 20) / (static_cast<int64_t>(kBM) * K);
+  int64_t gm = (24ll << 20) / (static_cast<int64_t>(tile_m) * K);
   if (gm < 1) gm = 1;
   if (gm > p.m_tiles) gm = p.m_tiles;
   p.group_m = static_cast<int>(gm);
@@ -287,10 +352,22 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
 
   auto s = static_cast<cudaStream_t>(stream);
   const bool gelu = e.gelu_tanh != 0, requant = e.requant_q != nullptr;
+  if (use_pair) {
+    if (gelu && requant) return gemm_pair_launch<true, true>(d, ma, mb, mlx, mlb, p, s);
+    if (gelu) return gemm_pair_launch<true, false>(d, ma, mb, mlx, mlb, p, s);
+    if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, p, s);
+    return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, p, s);
+  }
   if (gelu && requant) return gemm_launch<true, true>(d, ma, mb, mlx, mlb, p, s);
   if (gelu) return gemm_launch<true, false>(d, ma, mb, mlx, mlb, p, s);
   if (requant) return gemm_launch<false, true>(d, ma, mb, mlx, mlb, p, s);
   return gemm_launch<false, false>(d, ma, mb, mlx, mlb, p, s);
+}
+
+int ltxfp8_gemm_set_variant(int variant) {
+  if (variant < 0 || variant > 2) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm_set_variant: unknown variant %d", variant);
+  g_gemm_variant.store(variant);
+  return LTXFP8_OK;
 }
 
 int ltxfp8_lora_a(const void* x, const void* lora_a, void* ax, int64_t M, int64_t K, int64_t r, void* stream) {

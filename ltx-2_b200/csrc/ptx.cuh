@@ -192,6 +192,21 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, uint32_t m
          | ((m >> 4) << 24);            // M >> 4
 }
 
+// ---------------------------------------------------------------- cp.async (4-byte scale prefetch)
+__device__ __forceinline__ void cp_async_4(uint32_t smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float lds_f32(uint32_t smem_addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(smem_addr) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------- clusters and CTA pairs
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -213,7 +228,7 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
 
 // Arrive on an mbarrier that may live in another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-D tile load into this CTA's shared memory whose completion is counted on the
@@ -308,6 +323,23 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {
   return r;
 }
 
+// 8 packed bf16 (one 16 B chunk) -> fp32 (exact).
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// As f32x2_to_e4m3x2 for products x * s with a finite scale s: |x * s| <= 448
+// then holds for every element of the group (s = 448 / amax rounded), so the
+// saturating hardware conversion already equals torch's.
+__device__ __forceinline__ uint16_t f32x2_to_e4m3x2_inrange(float lo, float hi) {
+  return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -315,14 +347,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// GELU with the tanh approximation, in fp32, the formula torch evaluates for
-// F.gelu(x, approximate="tanh"): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+// GELU with the tanh approximation, the function torch evaluates for
+// F.gelu(x, approximate="tanh"): 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3).
+// Evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)), i.e.
+// gelu = x / (1 + exp(-2u)), with the fast exp and divide intrinsics (relative
+// error ~1e-6, far below the bf16 rounding the result goes through).  Unlike
+// 1 + tanh(u) the identity has no cancellation for negative x.
 __device__ __forceinline__ float gelu_tanh_f32(float x) {
   const float kBeta = 0.7978845608028654f;
   const float kKappa = 0.044715f;
-  const float x3 = x * x * x;
-  const float inner = kBeta * fmaf(kKappa, x3, x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float u = kBeta * fmaf(kKappa * x * x, x, x);
+  return __fdividef(x, 1.0f + __expf(-2.0f * u));
 }
 
 }  // namespace ltxfp8

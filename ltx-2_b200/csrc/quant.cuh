@@ -15,14 +15,6 @@ enum QuantMode : int {
 constexpr int kQuantRowsPerBlock = 16;   // 16 lanes per 128-group, 16 groups per 256-thread block
 constexpr int kQuantGroupsPerThread = 4; // groups in flight per thread (4 x 16 B loads)
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
 
 // Scale pair for one group from its abs-max.
 template <int kMode>

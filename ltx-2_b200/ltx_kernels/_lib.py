@@ -64,6 +64,7 @@ SIGNATURES = {
     "ltxfp8_dequantize_1x128": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "ltxfp8_gemm": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.POINTER(Epilogue), _vp]),
     "ltxfp8_lora_a": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ltxfp8_gemm_set_variant": (_i32, [_i32]),
     "ltxfp8_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _i32, _vp]),
 }
 
@@ -98,3 +99,13 @@ def device_status(stream: int = 0, clear: bool = True) -> int:
     st = ctypes.c_uint(0)
     check(load().ltxfp8_device_status(ctypes.byref(st), 1 if clear else 0, stream))
     return st.value
+
+
+GEMM_AUTO = 0
+GEMM_ONE_CTA = 1
+GEMM_CTA_PAIR = 2
+
+
+def set_gemm_variant(variant: int) -> None:
+    """Force the GEMM kernel (GEMM_AUTO, GEMM_ONE_CTA, GEMM_CTA_PAIR); process-wide."""
+    check(load().ltxfp8_gemm_set_variant(variant))

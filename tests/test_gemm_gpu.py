@@ -222,3 +222,46 @@ def test_gemm_with_runtime_lora(cuda_device, r):
     # the LoRA term is not negligible, and without it the error would be large
     assert np.linalg.norm(lora_only) / np.linalg.norm(ref) > 0.05
     assert m["rel_fro"] < 5e-3
+
+
+# --------------------------------------------------------------------------- both kernels on every shape class
+@pytest.fixture
+def gemm_variant():
+    from ltx_kernels import _lib
+    yield _lib.set_gemm_variant
+    _lib.set_gemm_variant(_lib.GEMM_AUTO)
+
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["one_cta", "cta_pair"])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 128), (100, 384, 256), (128, 256, 512), (129, 640, 384),
+                                   (300, 1024, 1024), (513, 256, 2048)])
+def test_gemm_kernel_variants(cuda_device, gemm_variant, variant, M, N, K):
+    from ltx_kernels.blockwise import ops
+    gemm_variant(variant)
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=M + N)
+    d = ops.gemm(aq, asc, wq, wsc, b)
+    torch.cuda.synchronize()
+    m = _check(d, _oracle(aq, asc, wq, wsc, b))
+    assert m["rel_fro"] < 3e-3
+
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["one_cta", "cta_pair"])
+def test_fused_epilogues_variants(cuda_device, gemm_variant, variant):
+    """GELU + requant and LoRA through each kernel; both kernels agree bit-for-bit."""
+    from ltx_kernels.blockwise import ops
+    M, N, K, r = 300, 768, 1024, 32
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=77)
+    la, lb = make_lora(N, K, r, seed=78)
+    ax = ops.lora_a(x.to(cuda_device), la.to(cuda_device))
+    gemm_variant(variant)
+    d, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
+    oq, os_ = O.quant_act_1x128(bits(d))
+    assert O.codes_equal(bits(q), oq).all()
+    assert O.scales_equal(scales_mn(s, M), os_[:, :M]).all()
+    dl = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5)
+    gemm_variant(1 if variant == 2 else 2)
+    d2, q2, s2 = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
+    dl2 = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5)
+    # Same promotion order in both kernels: identical results.
+    assert torch.equal(d, d2) and torch.equal(q.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s, s2)
+    assert torch.equal(dl, dl2)
