@@ -69,11 +69,17 @@ __global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat1
     }
     float s, inv;
     group_scale<kMode>(amax, s, inv);
+    // A finite scale keeps every |x * s| <= 448, where the saturating hardware
+    // conversion equals torch's; only non-finite scales need torch's overflow-to-NaN
+    // patch.  The Triton kernel converts with the saturating instruction throughout.
+    const bool in_range = (kMode == kQuantTriton) || isfinite(s);
     uint32_t w[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(f[4 * i], s), __fmul_rn(f[4 * i + 1], s));
-      const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(f[4 * i + 2], s), __fmul_rn(f[4 * i + 3], s));
+      const float v0 = __fmul_rn(f[4 * i], s), v1 = __fmul_rn(f[4 * i + 1], s);
+      const float v2 = __fmul_rn(f[4 * i + 2], s), v3 = __fmul_rn(f[4 * i + 3], s);
+      const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+      const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
       w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
     }
     if (row_ok && kb < KB) {
