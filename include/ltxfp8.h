@@ -132,6 +132,17 @@ int ltxfp8_lora_a(const void* x, const void* lora_a, void* ax, int64_t M, int64_
  */
 int ltxfp8_device_status(unsigned int* status, int clear, void* stream);
 
+/*
+ * Failure-path self-test: launches one warp that waits, with a limit of
+ * `limit_ns`, on a barrier nothing arrives on; the bounded wait gives up,
+ * records 0x5E1F0001 in the device status word and the kernel returns.
+ * Synchronises `stream`; *status receives the word (then cleared).  Shows that
+ * a stuck pipeline ends with an error the host can read, not a hung GPU.
+ * No reference counterpart (the reference's IPC barrier traps on timeout,
+ * ltx-kernels/csrc/include/cuda/utils.cuh:264-295).
+ */
+int ltxfp8_selftest_wait_timeout(unsigned long long limit_ns, unsigned int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

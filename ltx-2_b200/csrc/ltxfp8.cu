@@ -188,6 +188,21 @@ int gemm_pair_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, 
   return LTXFP8_OK;
 }
 
+// Self-test of the failure path: one warp waits on an mbarrier nothing will
+// arrive on, with a short limit; the bounded wait records kStSelftest and the
+// kernel returns normally.
+constexpr unsigned int kStSelftest = 0x5E1F0001u;
+
+__global__ void selftest_wait_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+  }
+  __syncwarp();
+  (void)mbar_wait(&bar, 0u, kStSelftest, limit_ns);
+}
+
 }  // namespace
 
 extern "C" {
@@ -305,7 +320,7 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   const bool use_pair = variant == 2;
   const int tile_m = use_pair ? pair::kTileM : kBM;
   const int tile_n = use_pair ? pair::kTileN : kBN;
-  const uint32_t w_rows_per_load = use_pair ? pair::kRowsPerCta : kBN;  // N rows each CTA loads
+  const uint32_t w_rows_per_load = use_pair ? pair::kRowsPerCta : kBN;  // W rows each CTA loads
 
   CUtensorMap ma, mb, mlx, mlb;
   rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, K, kBK, kBM);
@@ -414,6 +429,24 @@ int ltxfp8_lora_a(const void* x, const void* lora_a, void* ax, int64_t M, int64_
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "lora_a launch");
   return LTXFP8_OK;
+}
+
+int ltxfp8_selftest_wait_timeout(unsigned long long limit_ns, unsigned int* status, void* stream) {
+  if (!status) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "selftest: null pointer");
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(LTXFP8_ERR_INVALID_ARGUMENT, "selftest: limit must be in (0, 10 s]");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  unsigned int prior = 0;
+  rc = ltxfp8_device_status(&prior, 1, stream);  // start from a clear word
+  if (rc) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  selftest_wait_kernel<<<1, 32, 0, s>>>(limit_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest");
+  return ltxfp8_device_status(status, 1, stream);
 }
 
 int ltxfp8_device_status(unsigned int* status, int clear, void* stream) {

@@ -66,6 +66,7 @@ SIGNATURES = {
     "ltxfp8_lora_a": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ltxfp8_gemm_set_variant": (_i32, [_i32]),
     "ltxfp8_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _i32, _vp]),
+    "ltxfp8_selftest_wait_timeout": (_i32, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint), _vp]),
 }
 
 
@@ -98,6 +99,16 @@ def device_status(stream: int = 0, clear: bool = True) -> int:
     """Read (and by default clear) the kernels' device status word; 0 = healthy."""
     st = ctypes.c_uint(0)
     check(load().ltxfp8_device_status(ctypes.byref(st), 1 if clear else 0, stream))
+    return st.value
+
+
+SELFTEST_STATUS = 0x5E1F0001
+
+
+def selftest_wait_timeout(limit_ns: int, stream: int = 0) -> int:
+    """Run the bounded-wait failure self-test; returns the status word it left."""
+    st = ctypes.c_uint(0)
+    check(load().ltxfp8_selftest_wait_timeout(limit_ns, ctypes.byref(st), stream))
     return st.value
 
 

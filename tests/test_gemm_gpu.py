@@ -265,3 +265,50 @@ def test_fused_epilogues_variants(cuda_device, gemm_variant, variant):
     # Same promotion order in both kernels: identical results.
     assert torch.equal(d, d2) and torch.equal(q.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s, s2)
     assert torch.equal(dl, dl2)
+
+
+def test_bounded_wait_failure_path(cuda_device):
+    """A barrier nothing arrives on: the kernel's wait gives up after ~1 s, records a
+    status the host reads, and the context stays usable for the next GEMM."""
+    import time
+    from ltx_kernels import _lib
+    from ltx_kernels.blockwise import ops
+    t0 = time.time()
+    st = _lib.selftest_wait_timeout(1_000_000_000, torch.cuda.current_stream().cuda_stream)
+    dt = time.time() - t0
+    assert st == _lib.SELFTEST_STATUS
+    assert 0.9 < dt < 30
+    assert ops.device_status() == 0          # read-and-clear left the word clean
+    x, aq, asc, wq, wsc, b = _problem(64, 256, 256, cuda_device, seed=90)
+    d = ops.gemm(aq, asc, wq, wsc, b)
+    _check(d, _oracle(aq, asc, wq, wsc, b))
+
+
+def test_gemm_in_cuda_graph(cuda_device):
+    """The C ABI neither allocates nor synchronises: a captured graph replays the
+    quantiser and both GEMM epilogues with results identical to eager launches."""
+    from ltx_kernels.blockwise import ops
+    M, K, N = 256, 512, 384
+    x = activations(M, K, seed=91).to(cuda_device)
+    wq, wsc = ops.quantize_weight_128x128(weights(N, K, seed=92).to(cuda_device))
+    b = make_bias(N).to(cuda_device)
+
+    def run():
+        aq, asc = ops.quantize_1x128(x)
+        d = ops.gemm(aq, asc, wq, wsc, b)
+        _, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=False)
+        return d, q, s
+
+    eager = run()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = run()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out[0], eager[0])
+    assert torch.equal(out[1].view(torch.uint8), eager[1].view(torch.uint8)) and torch.equal(out[2], eager[2])
