@@ -91,6 +91,8 @@ typedef struct ltxfp8_epilogue {
   const void* lora_b;     /* bf16 [N, lora_r], the LoRA up projection */
   int64_t lora_r;         /* rank, multiple of 16, <= 256 */
   float lora_alpha;       /* scale of the LoRA term */
+  void* workspace;        /* optional fp32 scratch for split-K on skinny M (see ltxfp8_gemm_workspace_bytes) */
+  size_t workspace_bytes; /* its size; split-K is used only when it is large enough */
 } ltxfp8_epilogue;
 
 /*
@@ -107,6 +109,15 @@ typedef struct ltxfp8_epilogue {
 int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
                 const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
                 void* stream);
+
+/*
+ * Scratch bytes ltxfp8_gemm would use for split-K at this shape on the current
+ * device (0 when the shape has enough output tiles to fill the GPU without it).
+ * Skinny GEMMs (few 128 x 256 output tiles) divide each tile's K blocks among
+ * several CTAs, write fp32 partials to the workspace and reduce them in a fixed
+ * order (deterministic).  No reference counterpart (the SM89 kernel has no split-K).
+ */
+int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes);
 
 /*
  * Select the GEMM kernel: 0 = default (the one-CTA kernel), 1 = the one-CTA

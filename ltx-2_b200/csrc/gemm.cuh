@@ -79,6 +79,12 @@ struct GemmParams {
   int64_t s_out_ld;
   float lora_alpha;
   int flags;
+  // Split-K for skinny M: each output tile's K blocks are divided among k_splits
+  // work units; unit partials (fp32, no bias) go to ws[split][M][N] and
+  // splitk_reduce_kernel sums them in split order.  k_splits = 1: no split.
+  int k_splits;
+  int kb_per_split;
+  float* ws;
 };
 
 // Grouped rasterisation: consecutive tile indices walk group_m M-tiles down a
@@ -91,6 +97,23 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, const GemmParams& p, 
   const int r = tile - g * per_group;
   mt = first_m + r % gm;
   nt = r / gm;
+}
+
+// One work unit: an output tile and a contiguous range of its K blocks (the
+// whole range unless split-K is on); LoRA blocks ride with the last split.
+struct GemmUnit {
+  int mt, nt, split, kb_begin, n_fp8, n_blocks;
+};
+
+__device__ __forceinline__ GemmUnit gemm_unit(int u, const GemmParams& p) {
+  GemmUnit w;
+  const int tile = u / p.k_splits;
+  w.split = u - tile * p.k_splits;
+  gemm_tile_coords(tile, p, w.mt, w.nt);
+  w.kb_begin = w.split * p.kb_per_split;
+  w.n_fp8 = min(p.kb_per_split, p.num_kb - w.kb_begin);
+  w.n_blocks = w.n_fp8 + (w.split == p.k_splits - 1 ? p.num_lora : 0);
+  return w;
 }
 
 constexpr int kScalePrefetch = 4;
@@ -175,7 +198,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_blocks = p.num_kb + p.num_lora;
 
   if (warp < 4) {
     setmaxnreg_dec<kRegsCtrl>();
@@ -183,11 +205,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // ------------------------------------------------------------ TMA producer
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        int mt, nt;
-        gemm_tile_coords(tile, p, mt, nt);
-        const int m0 = mt * kBM, n0 = nt * kBN;
-        for (int kb = 0; kb < num_blocks; ++kb, ++it) {
+      const int total_units = p.total_tiles * p.k_splits;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        const GemmUnit w = gemm_unit(u, p);
+        const int m0 = w.mt * kBM, n0 = w.nt * kBN;
+        for (int kb = 0; kb < w.n_blocks; ++kb, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, kStProducerEmpty)) {
             ok = false;
@@ -196,11 +218,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* sa = smem + s * kStageBytes;
           uint8_t* sb = sa + kABytes;
           mbar_arrive_expect_tx(&full[s], kStageBytes);
-          if (kb < p.num_kb) {
-            tma_load_2d(&tmA, &full[s], sa, kb * kBK, m0);
-            tma_load_2d(&tmB, &full[s], sb, kb * kBK, n0);
+          if (kb < w.n_fp8) {
+            tma_load_2d(&tmA, &full[s], sa, (w.kb_begin + kb) * kBK, m0);
+            tma_load_2d(&tmB, &full[s], sb, (w.kb_begin + kb) * kBK, n0);
           } else {
-            const int c = (kb - p.num_kb) * kLoraChunk;
+            const int c = (kb - w.n_fp8) * kLoraChunk;
             tma_load_2d(&tmLX, &full[s], sa, c, m0);
             tma_load_2d(&tmLB, &full[s], sb, c, n0);
           }
@@ -217,8 +239,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t kIdescBF16 = make_idesc(1u, kBM, kBN);
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-        for (int kb = 0; kb < num_blocks; ++kb, ++it) {
+      const int total_units = p.total_tiles * p.k_splits;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        const GemmUnit w = gemm_unit(u, p);
+        for (int kb = 0; kb < w.n_blocks; ++kb, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
           const uint32_t buf = it & 1u, bph = (it >> 1) & 1u;
           if (!mbar_wait(&tempty[buf], bph ^ 1u, kStMmaTmemEmpty)) {
@@ -235,7 +259,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t adesc = sw128_kmajor_desc(a_addr);
           const uint64_t bdesc = sw128_kmajor_desc(a_addr + kABytes);
           const uint32_t d_tmem = tmem_base + buf * kBN;
-          if (kb < p.num_kb) {
+          if (kb < w.n_fp8) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)  // 4 x K32 (32 B of each 128 B row)
               mma_f8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, kIdescF8, j > 0 ? 1u : 0u);
@@ -259,16 +283,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 4) >> 2; // which 128-column half of the 256-wide tile
     uint32_t it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-      int mt, nt;
-      gemm_tile_coords(tile, p, mt, nt);
-      const int row = mt * kBM + sp * 32 + lane;
+    const int total_units = p.total_tiles * p.k_splits;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const GemmUnit w = gemm_unit(u, p);
+      const int row = w.mt * kBM + sp * 32 + lane;
       const bool row_ok = row < p.M;
-      const int col0 = nt * kBN + half * 128;
+      const int col0 = w.nt * kBN + half * 128;
       const bool col_ok = col0 < p.N;  // N % 128 == 0: a 128-column slab is all in or all out
       const int nb = col0 / 128;
-      const float* sfa_row = p.sfa + row;
-      const float* sfb_blk = p.sfb + static_cast<int64_t>(nb) * p.num_kb;
+      const float* sfa_row = p.sfa + row + static_cast<int64_t>(w.kb_begin) * p.sfa_ld;
+      const float* sfb_blk = p.sfb + static_cast<int64_t>(nb) * p.num_kb + w.kb_begin;
 
       float2 acc[64];  // column pairs (2j, 2j+1) of this thread's row
 #pragma unroll
@@ -281,18 +305,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       float sa[kScalePrefetch], sb[kScalePrefetch];
 #pragma unroll
       for (int j = 0; j < kScalePrefetch; ++j) {
-        sa[j] = (row_ok && j < p.num_kb) ? __ldg(sfa_row + static_cast<int64_t>(j) * p.sfa_ld) : 0.f;
-        sb[j] = (col_ok && j < p.num_kb) ? __ldg(sfb_blk + j) : 0.f;
+        sa[j] = (row_ok && j < w.n_fp8) ? __ldg(sfa_row + static_cast<int64_t>(j) * p.sfa_ld) : 0.f;
+        sb[j] = (col_ok && j < w.n_fp8) ? __ldg(sfb_blk + j) : 0.f;
       }
-      for (int kb0 = 0; kb0 < num_blocks && ok; kb0 += kScalePrefetch) {
+      for (int kb0 = 0; kb0 < w.n_blocks && ok; kb0 += kScalePrefetch) {
 #pragma unroll
         for (int j = 0; j < kScalePrefetch; ++j) {
           const int kb = kb0 + j;
-          if (kb < num_blocks && ok) {
-            const float scale = kb < p.num_kb ? sa[j] * sb[j] : p.lora_alpha;
+          if (kb < w.n_blocks && ok) {
+            const float scale = kb < w.n_fp8 ? sa[j] * sb[j] : p.lora_alpha;
             const int kn = kb + kScalePrefetch;
-            sa[j] = (row_ok && kn < p.num_kb) ? __ldg(sfa_row + static_cast<int64_t>(kn) * p.sfa_ld) : 0.f;
-            sb[j] = (col_ok && kn < p.num_kb) ? __ldg(sfb_blk + kn) : 0.f;
+            sa[j] = (row_ok && kn < w.n_fp8) ? __ldg(sfa_row + static_cast<int64_t>(kn) * p.sfa_ld) : 0.f;
+            sb[j] = (col_ok && kn < w.n_fp8) ? __ldg(sfb_blk + kn) : 0.f;
             ok = promote_kblock(tfull, tempty, tmem_base, sp, half, it, scale, lane, acc);
             ++it;
           }
@@ -300,6 +324,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok) break;
       if (!(row_ok && col_ok)) continue;
+      if (p.k_splits > 1) {
+        // Split-K unit: the raw fp32 partial (no bias) for the reduction kernel.
+        float4* dst = reinterpret_cast<float4*>(p.ws + (static_cast<int64_t>(w.split) * p.M + row) * p.N + col0);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dst[c] = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
+        continue;
+      }
       float* accf = reinterpret_cast<float*>(acc);
 
       // ------------------------------------------------ bias (+ GELU) in fp32, bf16 rounding
@@ -365,6 +396,76 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Split-K reduction: out = epilogue( sum_split ws[split] + bias ), summing the
+// unit partials in split order (deterministic).  One half-warp per (row,
+// 128-column group): 16 lanes x 8 columns, so the 1x128 requantisation needs no
+// cross-row reduction.  Epilogue semantics are those of the GEMM kernel.
+template <bool kGelu, bool kRequant>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmParams p) {
+  const int groups_per_row = p.N / 128;
+  const int64_t total = static_cast<int64_t>(p.M) * groups_per_row;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);
+  const int l16 = threadIdx.x & 15;
+  const bool active = gid < total;
+  const int row = active ? static_cast<int>(gid / groups_per_row) : 0;
+  const int grp = active ? static_cast<int>(gid - static_cast<int64_t>(row) * groups_per_row) : 0;
+  const int col = grp * 128 + l16 * 8;
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = 0.f;
+  if (active) {
+    const int64_t split_stride = static_cast<int64_t>(p.M) * p.N;
+    const float* src = p.ws + static_cast<int64_t>(row) * p.N + col;
+    for (int sp = 0; sp < p.k_splits; ++sp) {
+      const float4 a = *reinterpret_cast<const float4*>(src + sp * split_stride);
+      const float4 b = *reinterpret_cast<const float4*>(src + sp * split_stride + 4);
+      f[0] += a.x; f[1] += a.y; f[2] += a.z; f[3] += a.w;
+      f[4] += b.x; f[5] += b.y; f[6] += b.z; f[7] += b.w;
+    }
+    if (p.flags & kGemmBias) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(p.bias + col));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col + 4));
+      f[0] += a.x; f[1] += a.y; f[2] += a.z; f[3] += a.w;
+      f[4] += b.x; f[5] += b.y; f[6] += b.z; f[7] += b.w;
+    }
+  }
+  if constexpr (kGelu || kRequant) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float y = bf16_round(f[i]);
+      if constexpr (kGelu) y = bf16_round(gelu_tanh_f32(y));
+      f[i] = y;
+    }
+  }
+  const int64_t off = static_cast<int64_t>(row) * p.N + col;
+  if (active && (p.flags & kGemmWriteD)) {
+    *reinterpret_cast<uint4*>(p.d + off) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                                      pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+  if constexpr (kRequant) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmax_nan(amax, fabsf(f[i]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o, 16));
+    const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
+    const bool in_range = isfinite(s);
+    uint32_t w[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float v0 = __fmul_rn(f[4 * j], s), v1 = __fmul_rn(f[4 * j + 1], s);
+      const float v2 = __fmul_rn(f[4 * j + 2], s), v3 = __fmul_rn(f[4 * j + 3], s);
+      const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+      const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
+      w[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    if (active) {
+      *reinterpret_cast<uint2*>(p.q_out + off) = make_uint2(w[0], w[1]);
+      if (l16 == 0) p.s_out[static_cast<int64_t>(grp) * p.s_out_ld + row] = __frcp_rn(s);
+    }
   }
 }
 

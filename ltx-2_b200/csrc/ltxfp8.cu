@@ -133,13 +133,47 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
                 const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
   int rc = gemm_prepare<kGelu, kRequant>(d);
   if (rc) return rc;
-  const int grid = p.total_tiles < d->sms ? p.total_tiles : d->sms;
+  const int units = p.total_tiles * p.k_splits;
+  const int grid = units < d->sms ? units : d->sms;
   fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return LTXFP8_OK;
 }
 
+
+// Split-K plan for the one-CTA kernel: enough work units to cover the SMs,
+// at least two K blocks per unit, at most 16 units per tile.
+int splitk_plan(const DeviceInfo* d, int64_t total_tiles, int64_t num_kb, int* kb_per_split) {
+  *kb_per_split = static_cast<int>(num_kb);
+  if (total_tiles * 2 > d->sms || num_kb < 4) return 1;
+  int64_t want = (d->sms + total_tiles - 1) / total_tiles;
+  if (want > num_kb / 2) want = num_kb / 2;
+  if (want > 16) want = 16;
+  if (want < 2) return 1;
+  const int64_t kbps = (num_kb + want - 1) / want;
+  *kb_per_split = static_cast<int>(kbps);
+  return static_cast<int>((num_kb + kbps - 1) / kbps);
+}
+
+template <bool kGelu, bool kRequant>
+int splitk_reduce_launch(const DeviceInfo* d, const GemmParams& p, cudaStream_t stream) {
+  const int64_t groups = static_cast<int64_t>(p.M) * (p.N / 128);
+  const unsigned blocks = static_cast<unsigned>((groups + 15) / 16);
+  splitk_reduce_kernel<kGelu, kRequant><<<blocks, 256, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
+  (void)d;
+  return LTXFP8_OK;
+}
+
+template <bool kGelu, bool kRequant>
+int gemm_launch_full(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
+                     const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
+  int rc = gemm_launch<kGelu, kRequant>(d, a, b, lx, lb, p, stream);
+  if (rc || p.k_splits == 1) return rc;
+  return splitk_reduce_launch<kGelu, kRequant>(d, p, stream);
+}
 
 template <bool kGelu, bool kRequant>
 int gemm_pair_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
@@ -366,6 +400,20 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   p.s_out_ld = e.requant_ld;
   p.lora_alpha = e.lora_alpha;
   p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0);
+  p.k_splits = 1;
+  p.kb_per_split = p.num_kb;
+  p.ws = nullptr;
+  if (!use_pair && e.workspace) {
+    int kbps = p.num_kb;
+    const int splits = splitk_plan(d, p.total_tiles, p.num_kb, &kbps);
+    const size_t need = static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4u;
+    if (splits > 1 && need <= e.workspace_bytes) {
+      if (!aligned(e.workspace, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: workspace must be 16-byte aligned");
+      p.k_splits = splits;
+      p.kb_per_split = kbps;
+      p.ws = static_cast<float*>(e.workspace);
+    }
+  }
 
   auto s = static_cast<cudaStream_t>(stream);
   const bool gelu = e.gelu_tanh != 0, requant = e.requant_q != nullptr;
@@ -375,10 +423,25 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
     if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, p, s);
     return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, p, s);
   }
-  if (gelu && requant) return gemm_launch<true, true>(d, ma, mb, mlx, mlb, p, s);
-  if (gelu) return gemm_launch<true, false>(d, ma, mb, mlx, mlb, p, s);
-  if (requant) return gemm_launch<false, true>(d, ma, mb, mlx, mlb, p, s);
-  return gemm_launch<false, false>(d, ma, mb, mlx, mlb, p, s);
+  if (gelu && requant) return gemm_launch_full<true, true>(d, ma, mb, mlx, mlb, p, s);
+  if (gelu) return gemm_launch_full<true, false>(d, ma, mb, mlx, mlb, p, s);
+  if (requant) return gemm_launch_full<false, true>(d, ma, mb, mlx, mlb, p, s);
+  return gemm_launch_full<false, false>(d, ma, mb, mlx, mlb, p, s);
+}
+
+int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) {
+  if (!bytes) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm_workspace_bytes: null pointer");
+  *bytes = 0;
+  if (M < 1 || N < 128 || K < 128 || N % 128 != 0 || K % 128 != 0) return LTXFP8_OK;
+  if (g_gemm_variant.load() == 2) return LTXFP8_OK;
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  int kbps = 0;
+  const int splits = splitk_plan(d, tiles, K / kBK, &kbps);
+  if (splits > 1) *bytes = static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4u;
+  return LTXFP8_OK;
 }
 
 int ltxfp8_gemm_set_variant(int variant) {

@@ -51,6 +51,8 @@ class Epilogue(ctypes.Structure):
         ("lora_b", ctypes.c_void_p),
         ("lora_r", ctypes.c_int64),
         ("lora_alpha", ctypes.c_float),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -65,6 +67,7 @@ SIGNATURES = {
     "ltxfp8_gemm": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.POINTER(Epilogue), _vp]),
     "ltxfp8_lora_a": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ltxfp8_gemm_set_variant": (_i32, [_i32]),
+    "ltxfp8_gemm_workspace_bytes": (_i32, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
     "ltxfp8_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _i32, _vp]),
     "ltxfp8_selftest_wait_timeout": (_i32, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_uint), _vp]),
 }
@@ -120,3 +123,5 @@ GEMM_CTA_PAIR = 2
 def set_gemm_variant(variant: int) -> None:
     """Force the GEMM kernel (GEMM_AUTO, GEMM_ONE_CTA, GEMM_CTA_PAIR); process-wide."""
     check(load().ltxfp8_gemm_set_variant(variant))
+    from .blockwise import ops  # the split-K workspace size depends on the kernel
+    ops._WS_CACHE.clear()

@@ -132,12 +132,13 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
          bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,
          gelu: bool = False, requant: bool = False, write_d: bool = True,
          lora_ax: Optional[torch.Tensor] = None, lora_b: Optional[torch.Tensor] = None,
-         lora_alpha: float = 1.0):
+         lora_alpha: float = 1.0, split_k: bool = True):
     """Blockwise FP8 GEMM with fused epilogue.
 
     Returns D (bf16 [M, N]) when ``requant`` is False, else ``(D or None, q, scales)``
     where ``q``/``scales`` are the 1x128 quantisation of the (GELU'd) bf16 output in
-    the same layout blockwise::quantize produces."""
+    the same layout blockwise::quantize produces.  Skinny shapes get a split-K
+    workspace from the caching allocator unless ``split_k`` is False."""
     _require_cuda("gemm", a_q, sfa, w_q, sfb, bias, lora_ax, lora_b)
     if a_q.dim() != 2 or w_q.dim() != 2:
         raise RuntimeError("gemm expects 2-D operands")
@@ -185,12 +186,33 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
         ep.lora_r = r
         ep.lora_alpha = float(lora_alpha)
     with _DeviceGuard(a_q):
+        ws_bytes = gemm_workspace_bytes(M, N, K, a_q.device) if split_k else 0
+        ws = None
+        if ws_bytes:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a_q.device)
+            ep.workspace = ws.data_ptr()
+            ep.workspace_bytes = ws_bytes
         L.check(L.load().ltxfp8_gemm(a_q.data_ptr(), sfa.data_ptr(), ld, w_q.data_ptr(), sfb.data_ptr(),
                                      None if bias is None else bias.data_ptr(),
                                      None if d is None else d.data_ptr(), M, N, K, ep, _stream(a_q)))
     if requant:
         return d, q, s
     return d
+
+
+_WS_CACHE: dict = {}
+
+
+def gemm_workspace_bytes(M: int, N: int, K: int, device) -> int:
+    """Split-K scratch the GEMM would use at this shape (0 when it needs none)."""
+    key = (torch.cuda.current_device() if device is None else device.index, M, N, K)
+    v = _WS_CACHE.get(key)
+    if v is None:
+        import ctypes
+        n = ctypes.c_size_t(0)
+        L.check(L.load().ltxfp8_gemm_workspace_bytes(M, N, K, ctypes.byref(n)))
+        v = _WS_CACHE[key] = n.value
+    return v
 
 
 def lora_a(x: torch.Tensor, a: torch.Tensor) -> torch.Tensor:

@@ -254,15 +254,15 @@ def test_fused_epilogues_variants(cuda_device, gemm_variant, variant):
     la, lb = make_lora(N, K, r, seed=78)
     ax = ops.lora_a(x.to(cuda_device), la.to(cuda_device))
     gemm_variant(variant)
-    d, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
+    d, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True, split_k=False)
     oq, os_ = O.quant_act_1x128(bits(d))
     assert O.codes_equal(bits(q), oq).all()
     assert O.scales_equal(scales_mn(s, M), os_[:, :M]).all()
-    dl = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5)
+    dl = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5, split_k=False)
     gemm_variant(1 if variant == 2 else 2)
-    d2, q2, s2 = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
-    dl2 = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5)
-    # Same promotion order in both kernels: identical results.
+    d2, q2, s2 = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True, split_k=False)
+    dl2 = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5, split_k=False)
+    # Same promotion order in both kernels (no split-K): identical results.
     assert torch.equal(d, d2) and torch.equal(q.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s, s2)
     assert torch.equal(dl, dl2)
 
@@ -312,3 +312,40 @@ def test_gemm_in_cuda_graph(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(out[0], eager[0])
     assert torch.equal(out[1].view(torch.uint8), eager[1].view(torch.uint8)) and torch.equal(out[2], eager[2])
+
+
+# --------------------------------------------------------------------------- split-K for skinny M
+@pytest.mark.parametrize("M,N,K", [(1, 128, 1024), (100, 256, 4096), (128, 2048, 2048), (256, 4096, 4096),
+                                   (96, 384, 640)])
+def test_splitk_skinny_shapes(cuda_device, M, N, K):
+    from ltx_kernels.blockwise import ops
+    ws = ops.gemm_workspace_bytes(M, N, K, cuda_device)
+    assert ws > 0  # these shapes have few output tiles: split-K engages
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=K + M)
+    d = ops.gemm(aq, asc, wq, wsc, b)
+    d1 = ops.gemm(aq, asc, wq, wsc, b, split_k=False)
+    m = _check(d, _oracle(aq, asc, wq, wsc, b))
+    assert m["rel_fro"] < 3e-3
+    # split order differs from the single-unit promotion only by fp32 summation order
+    diff = (d.float() - d1.float()).abs().max().item()
+    assert diff <= 0.02 * d1.float().abs().max().item()
+    assert torch.equal(d, ops.gemm(aq, asc, wq, wsc, b))  # deterministic
+
+
+def test_splitk_fused_epilogues(cuda_device):
+    """GELU + requant and LoRA through the split-K reduction."""
+    from ltx_kernels.blockwise import ops
+    M, N, K, r = 128, 1024, 2048, 32
+    assert ops.gemm_workspace_bytes(M, N, K, cuda_device) > 0
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=123)
+    d, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
+    oq, os_ = O.quant_act_1x128(bits(d))
+    assert O.codes_equal(bits(q), oq).all()
+    assert O.scales_equal(scales_mn(s, M), os_[:, :M]).all()
+    ref = O.bf16_to_f32(O.gelu_tanh_bf16(O.f32_to_bf16(_oracle(aq, asc, wq, wsc, b))))
+    _check(d, ref)
+    la, lb = make_lora(N, K, r, seed=124)
+    ax = ops.lora_a(x.to(cuda_device), la.to(cuda_device))
+    dl = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5)
+    ref = _oracle(aq, asc, wq, wsc, b) + O.lora_exact_f32(bits(x), bits(la), bits(lb), 0.5)
+    _check(dl, ref)
