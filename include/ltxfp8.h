@@ -120,6 +120,27 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
 int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes);
 
 /*
+ * ltxfp8_gemm for callers that cannot allocate device memory per call: a host
+ * whose memory is all owned by its own arena or a framework's allocator, or a
+ * plugin whose launch hook (an enqueue or execute callback) must not allocate.
+ * Same arguments, results and errors as ltxfp8_gemm; ep->workspace and
+ * ep->workspace_bytes are ignored.  The split-K scratch of skinny shapes comes
+ * from one fixed 32 MiB array in the library's device globals instead of the
+ * caller: every GPU that loads the library's kernels holds those 32 MiB until
+ * the process exits.  A shape whose split-K plan needs more than 32 MiB returns
+ * LTXFP8_ERR_UNSUPPORTED_SHAPE (none does on a 148-SM B200).
+ * The first call on each device looks up the array's device address, with
+ * that device current; make that first call before any stream capture.
+ * All calls on a device share the array and it keeps the last call's partials
+ * (nothing in it needs to start at zero): calls that can overlap on the GPU
+ * (other streams, other host threads) race on it, so issue them on one stream.
+ * No reference counterpart.
+ */
+int ltxfp8_gemm_static_scratch(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                               const float* bias, void* D, int64_t M, int64_t N, int64_t K,
+                               const ltxfp8_epilogue* ep, void* stream);
+
+/*
  * Select the GEMM kernel: 0 = default (the one-CTA kernel), 1 = the one-CTA
  * kernel (128 x 256 tiles per SM), 2 = the CTA-pair kernel (256 x 256 tiles
  * over two SMs of a cluster, tcgen05 cta_group::2).  Process-wide; meant for tests and tuning.  No reference

@@ -21,6 +21,16 @@
 
 using namespace ltxfp8;
 
+// Split-K scratch of ltxfp8_gemm_static_scratch: a fixed 32 MiB array in the
+// module's global memory, so that entry point needs no allocation.  Every GPU
+// that loads this library's kernels holds it until the process exits.  32 MiB
+// covers the split-K plan of every shape on a 148-SM device: a split is used
+// only while the output has at most sms/2 tiles of 128 x 256, and the plan makes
+// splits x tiles <= sms + tiles - 1, so the fp32 partials take at most
+// (148 + 73) x 128 x 256 x 4 bytes = 27.6 MiB.
+constexpr size_t kStaticScratchBytes = 32ull << 20;
+static __device__ __align__(256) float g_gemm_static_scratch[kStaticScratchBytes / sizeof(float)];
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -80,6 +90,7 @@ struct DeviceInfo {
   bool pair_ready[4] = {false, false, false, false};
   int pair_clusters = 0;  // co-resident 2-CTA clusters of the pair kernel
   bool lora_ready = false;
+  float* static_scratch = nullptr;  // device address of g_gemm_static_scratch (ltxfp8_gemm_static_scratch)
 };
 
 // 0 = choose by shape, 1 = one-CTA kernel, 2 = CTA-pair kernel.
@@ -442,6 +453,42 @@ int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) 
   const int splits = splitk_plan(d, tiles, K / kBK, &kbps);
   if (splits > 1) *bytes = static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4u;
   return LTXFP8_OK;
+}
+
+int ltxfp8_gemm_static_scratch(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                               const float* bias, void* D, int64_t M, int64_t N, int64_t K,
+                               const ltxfp8_epilogue* ep, void* stream) {
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  {
+    // Once per device, with that device current: the device address of the array.
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!d->static_scratch) {
+      void* ptr = nullptr;
+      cudaError_t err = cudaGetSymbolAddress(&ptr, g_gemm_static_scratch);
+      if (err != cudaSuccess) return cuda_fail(err, "gemm_static_scratch: cudaGetSymbolAddress");
+      d->static_scratch = static_cast<float*>(ptr);
+    }
+  }
+  size_t need = 0;
+  rc = ltxfp8_gemm_workspace_bytes(M, N, K, &need);
+  if (rc) return rc;
+  if (need > kStaticScratchBytes)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE,
+                "gemm_static_scratch: M=%lld N=%lld K=%lld needs %zu bytes of split-K scratch, the static array holds %zu",
+                (long long)M, (long long)N, (long long)K, need, kStaticScratchBytes);
+  ltxfp8_epilogue e;
+  if (ep) {
+    e = *ep;
+  } else {
+    memset(&e, 0, sizeof(e));
+  }
+  // Each split writes every partial the reduction reads before the reduction
+  // runs, so nothing in the array has to start at zero.
+  e.workspace = need ? d->static_scratch : nullptr;
+  e.workspace_bytes = need ? kStaticScratchBytes : 0;
+  return ltxfp8_gemm(A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, &e, stream);
 }
 
 int ltxfp8_gemm_set_variant(int variant) {
