@@ -80,6 +80,54 @@ int ltxfp8_quantize_weight_128x128(const void* w, int dtype, int64_t N, int64_t 
 int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stride, int64_t col_stride, int64_t M,
                             int64_t K, void* out, void* stream);
 
+/*
+ * Fused producers of the GEMM's A operand.  Rows are tokens of a [B, S, H]
+ * bf16 tensor with contiguous rows (row stride H), M = B * S, H % 128 == 0,
+ * H <= 8192.  Per-batch/per-token parameter tensors are addressed as
+ * p[b * bstride + s * sstride + h] (sstride 0 broadcasts over the S tokens).
+ * Quantised outputs use the layout of ltxfp8_quantize_1x128 with q_ld = H;
+ * flags selects the quantiser arithmetic (LTXFP8_QUANT_*).  Row sums of squares
+ * are accumulated in fp32 in a fixed order and 1/sqrt is an IEEE sqrt and
+ * division (the reference sums the bf16 squares in bf16 and uses the fast rsqrt).
+ */
+
+/*
+ * AdaLN producer: y = bf16(x * rsqrt(mean(bf16(x^2)) + 1e-5));
+ * z = bf16(bf16(y * bf16(1 + scale)) + shift); (q, sfa) = 1x128 quant of z.
+ * scale, shift bf16.  Replaces blockwise::adanorm / blockwise_quantize_adanorm_triton
+ * (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:52-96,158-186).
+ */
+int ltxfp8_adanorm_quantize(const void* x, int64_t B, int64_t S, int64_t H, const void* scale,
+                            int64_t scale_bstride, int64_t scale_sstride, const void* shift, int64_t shift_bstride,
+                            int64_t shift_sstride, void* q, float* sfa, int64_t sfa_ld, int flags, void* stream);
+
+/*
+ * Residual update + RMS norm: x <- bf16(x + bf16(y * z)) in place;
+ * o = x * rsqrt(mean(bf16(x^2))) in fp32 (no epsilon).  With q != NULL,
+ * (q, sfa) = 1x128 quant of o (blockwise::quant_rms_fma); otherwise out = bf16(o)
+ * (blockwise::rms_fma).  y bf16 [M, H], z bf16.
+ * Replaces _quant_rms_sum_mult_kernel and its two ops (triton_ops.py:188-290).
+ */
+int ltxfp8_rms_fma(void* x, const void* y, int64_t B, int64_t S, int64_t H, const void* z, int64_t z_bstride,
+                   int64_t z_sstride, void* q, float* sfa, int64_t sfa_ld, void* out, int flags, void* stream);
+
+/*
+ * Gated attention output: o = x * 2 sigmoid(gate_logits[m, h / (H / heads)]) in fp32,
+ * x bf16 [M, H], gate_logits [M, heads] of gate_dtype (LTXFP8_DTYPE_BF16 or _F32),
+ * (H / heads) % 8 == 0.  With q != NULL the 1x128 quant of o, otherwise out = bf16(o).
+ * Replaces blockwise::gated_attention / gated_attention_triton (triton_ops.py:293-345).
+ */
+int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtype, int64_t M, int64_t H,
+                           int64_t heads, void* q, float* sfa, int64_t sfa_ld, void* out, int flags, void* stream);
+
+/*
+ * GELU (sigmoid form) + quant: o = x * sigmoid(1.702 x) in fp32, then the 1x128
+ * quant of o; arguments as ltxfp8_quantize_1x128.  Replaces blockwise::quantize
+ * with use_gelu=True (triton_ops.py:98-100,102-151).
+ */
+int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld, float* sfa,
+                               int64_t sfa_ld, int flags, void* stream);
+
 /* Epilogue options of ltxfp8_gemm (all zero = plain bias + bf16 store). */
 typedef struct ltxfp8_epilogue {
   int gelu_tanh;          /* apply GELU (tanh approximation) to bf16(acc + bias), rounding to bf16 */

@@ -16,6 +16,7 @@
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
 #include "lora.cuh"
+#include "producers.cuh"
 #include "ptx.cuh"
 #include "quant.cuh"
 
@@ -248,6 +249,82 @@ __global__ void selftest_wait_kernel(unsigned long long limit_ns) {
   (void)mbar_wait(&bar, 0u, kStSelftest, limit_ns);
 }
 
+// Producers: per-row chunk count (16 B per lane per load) for a row of H bf16.
+int producer_chunks(int64_t H) {
+  const int64_t n = (H / 8 + 31) / 32;
+  return n <= 4 ? 4 : n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : 0;
+}
+
+int producer_check(const char* name, int64_t M, int64_t H, int flags) {
+  if (M < 0 || H <= 0 || H % 128 != 0 || H > 8192)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "%s: need H %% 128 == 0, 0 < H <= 8192, M >= 0 (M=%lld H=%lld)", name,
+                (long long)M, (long long)H);
+  if (M > (static_cast<int64_t>(1) << 31) * kProdWarps)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "%s: too many rows", name);
+  if (flags != LTXFP8_QUANT_TORCH && flags != LTXFP8_QUANT_TRITON)
+    return fail(LTXFP8_ERR_INVALID_ARGUMENT, "%s: unknown quant mode %d", name, flags);
+  return LTXFP8_OK;
+}
+
+int producer_out(const char* name, int64_t M, void* q, float* sfa, int64_t sfa_ld, void* out, bool allow_bf16,
+                 ProducerOut* o) {
+  o->q = static_cast<uint8_t*>(q);
+  o->sfa = sfa;
+  o->sfa_ld = sfa_ld;
+  o->out = static_cast<__nv_bfloat16*>(out);
+  if (q) {
+    if (!sfa) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "%s: sfa is null", name);
+    if (sfa_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "%s: sfa_ld < M", name);
+    if (!aligned(q, 16) || !aligned(sfa, 4)) return fail(LTXFP8_ERR_MISALIGNED, "%s: q must be 16-byte aligned", name);
+  } else {
+    if (!allow_bf16) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "%s: q is null", name);
+    if (!out) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "%s: need q or out", name);
+    if (!aligned(out, 16)) return fail(LTXFP8_ERR_MISALIGNED, "%s: out must be 16-byte aligned", name);
+  }
+  return LTXFP8_OK;
+}
+
+template <int kChunks, int kMode>
+void adanorm_launch(dim3 grid, cudaStream_t s, const __nv_bfloat16* x, int64_t M, int64_t S, int H,
+                    const __nv_bfloat16* sc, int64_t sc_bs, int64_t sc_ss, const __nv_bfloat16* sh, int64_t sh_bs,
+                    int64_t sh_ss, ProducerOut o) {
+  adanorm_quant_kernel<kChunks, kMode><<<grid, kProdWarps * 32, 0, s>>>(x, M, S, H, sc, sc_bs, sc_ss, sh, sh_bs,
+                                                                        sh_ss, o);
+}
+
+template <int kChunks, int kMode>
+void rms_fma_launch(dim3 grid, cudaStream_t s, __nv_bfloat16* x, const __nv_bfloat16* y, int64_t M, int64_t S, int H,
+                    const __nv_bfloat16* z, int64_t z_bs, int64_t z_ss, ProducerOut o) {
+  if (o.q)
+    rms_fma_kernel<kChunks, kMode, true><<<grid, kProdWarps * 32, 0, s>>>(x, y, M, S, H, z, z_bs, z_ss, o);
+  else
+    rms_fma_kernel<kChunks, kMode, false><<<grid, kProdWarps * 32, 0, s>>>(x, y, M, S, H, z, z_bs, z_ss, o);
+}
+
+template <int kChunks, int kMode>
+void gated_launch(dim3 grid, cudaStream_t s, const __nv_bfloat16* x, const void* g, bool g_f32, int64_t M, int H,
+                  int heads, ProducerOut o) {
+  if (o.q) {
+    if (g_f32) gated_attention_kernel<kChunks, kMode, true, true><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
+    else gated_attention_kernel<kChunks, kMode, true, false><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
+  } else {
+    if (g_f32) gated_attention_kernel<kChunks, kMode, false, true><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
+    else gated_attention_kernel<kChunks, kMode, false, false><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
+  }
+}
+
+// Calls fn<kChunks, kMode>(args...) for the row length's chunk count and the mode.
+#define LTXFP8_PRODUCER_DISPATCH(fn, chunks, mode, ...)                        \
+  do {                                                                         \
+    const bool tri_ = (mode) == LTXFP8_QUANT_TRITON;                           \
+    switch (chunks) {                                                          \
+      case 4: tri_ ? fn<4, kQuantTriton>(__VA_ARGS__) : fn<4, kQuantTorch>(__VA_ARGS__); break;     \
+      case 8: tri_ ? fn<8, kQuantTriton>(__VA_ARGS__) : fn<8, kQuantTorch>(__VA_ARGS__); break;     \
+      case 16: tri_ ? fn<16, kQuantTriton>(__VA_ARGS__) : fn<16, kQuantTorch>(__VA_ARGS__); break;  \
+      default: tri_ ? fn<32, kQuantTriton>(__VA_ARGS__) : fn<32, kQuantTorch>(__VA_ARGS__); break;  \
+    }                                                                          \
+  } while (0)
+
 }  // namespace
 
 extern "C" {
@@ -321,6 +398,116 @@ int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stri
       static_cast<const uint8_t*>(q), scales, row_stride, col_stride, M, K, static_cast<__nv_bfloat16*>(out));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dequantize launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_adanorm_quantize(const void* x, int64_t B, int64_t S, int64_t H, const void* scale,
+                            int64_t scale_bstride, int64_t scale_sstride, const void* shift, int64_t shift_bstride,
+                            int64_t shift_sstride, void* q, float* sfa, int64_t sfa_ld, int flags, void* stream) {
+  if (B < 0 || S < 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "adanorm: negative B or S");
+  const int64_t M = B * S;
+  int rc = producer_check("adanorm", M, H, flags);
+  if (rc) return rc;
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !scale || !shift) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "adanorm: null pointer");
+  if (!aligned(x, 16) || !aligned(scale, 16) || !aligned(shift, 16) || scale_bstride % 8 || scale_sstride % 8 ||
+      shift_bstride % 8 || shift_sstride % 8)
+    return fail(LTXFP8_ERR_MISALIGNED, "adanorm: x, scale, shift must be 16-byte aligned with strides %% 8 == 0");
+  ProducerOut o;
+  rc = producer_out("adanorm", M, q, sfa, sfa_ld, nullptr, false, &o);
+  if (rc) return rc;
+  DeviceInfo* d;
+  rc = device_info(&d);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
+  LTXFP8_PRODUCER_DISPATCH(adanorm_launch, producer_chunks(H), flags, grid, static_cast<cudaStream_t>(stream),
+                           static_cast<const __nv_bfloat16*>(x), M, S, static_cast<int>(H),
+                           static_cast<const __nv_bfloat16*>(scale), scale_bstride, scale_sstride,
+                           static_cast<const __nv_bfloat16*>(shift), shift_bstride, shift_sstride, o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "adanorm launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_rms_fma(void* x, const void* y, int64_t B, int64_t S, int64_t H, const void* z, int64_t z_bstride,
+                   int64_t z_sstride, void* q, float* sfa, int64_t sfa_ld, void* out, int flags, void* stream) {
+  if (B < 0 || S < 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "rms_fma: negative B or S");
+  const int64_t M = B * S;
+  int rc = producer_check("rms_fma", M, H, flags);
+  if (rc) return rc;
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !y || !z) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "rms_fma: null pointer");
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(z, 16) || z_bstride % 8 || z_sstride % 8)
+    return fail(LTXFP8_ERR_MISALIGNED, "rms_fma: x, y, z must be 16-byte aligned with strides %% 8 == 0");
+  ProducerOut o;
+  rc = producer_out("rms_fma", M, q, sfa, sfa_ld, out, true, &o);
+  if (rc) return rc;
+  DeviceInfo* d;
+  rc = device_info(&d);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
+  LTXFP8_PRODUCER_DISPATCH(rms_fma_launch, producer_chunks(H), flags, grid, static_cast<cudaStream_t>(stream),
+                           static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), M, S,
+                           static_cast<int>(H), static_cast<const __nv_bfloat16*>(z), z_bstride, z_sstride, o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rms_fma launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtype, int64_t M, int64_t H,
+                           int64_t heads, void* q, float* sfa, int64_t sfa_ld, void* out, int flags, void* stream) {
+  int rc = producer_check("gated_attention", M, H, flags);
+  if (rc) return rc;
+  if (heads <= 0 || H % heads != 0 || (H / heads) % 8 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gated_attention: H / heads must be a multiple of 8 (H=%lld heads=%lld)",
+                (long long)H, (long long)heads);
+  if (gate_dtype != LTXFP8_DTYPE_BF16 && gate_dtype != LTXFP8_DTYPE_F32)
+    return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gated_attention: gate logits must be bf16 or fp32");
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !gate_logits) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gated_attention: null pointer");
+  if (!aligned(x, 16) || !aligned(gate_logits, gate_dtype == LTXFP8_DTYPE_F32 ? 4 : 2))
+    return fail(LTXFP8_ERR_MISALIGNED, "gated_attention: x must be 16-byte aligned");
+  ProducerOut o;
+  rc = producer_out("gated_attention", M, q, sfa, sfa_ld, out, true, &o);
+  if (rc) return rc;
+  DeviceInfo* d;
+  rc = device_info(&d);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
+  LTXFP8_PRODUCER_DISPATCH(gated_launch, producer_chunks(H), flags, grid, static_cast<cudaStream_t>(stream),
+                           static_cast<const __nv_bfloat16*>(x), gate_logits, gate_dtype == LTXFP8_DTYPE_F32, M,
+                           static_cast<int>(H), static_cast<int>(heads), o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gated_attention launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld, float* sfa,
+                               int64_t sfa_ld, int flags, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gelu_quantize: need K %% 128 == 0, K > 0, M >= 0 (M=%lld K=%lld)", (long long)M, (long long)K);
+  if (flags != LTXFP8_QUANT_TORCH && flags != LTXFP8_QUANT_TRITON) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gelu_quantize: unknown mode %d", flags);
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !q || !sfa) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gelu_quantize: null pointer");
+  if (x_ld < K || q_ld < K || sfa_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gelu_quantize: leading dimension too small");
+  if (!aligned(x, 16) || x_ld % 8 != 0) return fail(LTXFP8_ERR_MISALIGNED, "gelu_quantize: x must be 16-byte aligned with x_ld %% 8 == 0");
+  if (!aligned(q, 8) || q_ld % 8 != 0) return fail(LTXFP8_ERR_MISALIGNED, "gelu_quantize: q must be 8-byte aligned with q_ld %% 8 == 0");
+  if (!aligned(sfa, 4)) return fail(LTXFP8_ERR_MISALIGNED, "gelu_quantize: sfa must be 4-byte aligned");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t KB = K / 128;
+  dim3 grid(static_cast<unsigned>((M + kQuantRowsPerBlock - 1) / kQuantRowsPerBlock),
+            static_cast<unsigned>((KB + kQuantGroupsPerThread - 1) / kQuantGroupsPerThread));
+  if (grid.y > 65535u) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gelu_quantize: K too large");
+  auto s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* qb = static_cast<uint8_t*>(q);
+  if (flags == LTXFP8_QUANT_TRITON)
+    gelu_quant_kernel<kQuantTriton><<<grid, 256, 0, s>>>(xb, x_ld, M, KB, qb, q_ld, sfa, sfa_ld);
+  else
+    gelu_quant_kernel<kQuantTorch><<<grid, 256, 0, s>>>(xb, x_ld, M, KB, qb, q_ld, sfa, sfa_ld);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gelu_quantize launch");
   return LTXFP8_OK;
 }
 

@@ -1,0 +1,293 @@
+// Fused producers of the GEMM's A operand: per-token normalisation / gating
+// followed by the 1x128 e4m3 quantisation (HBM-bound streaming kernels).
+//
+//   adanorm_quant_kernel    RMSNorm (eps 1e-5) -> bf16 -> x * (1 + scale) + shift -> quant
+//                           (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:52-96,158-186)
+//   rms_fma_kernel          x <- x + y * z (in place), o = x * rsqrt(mean(x^2)) -> quant or bf16
+//                           (triton_ops.py:188-290)
+//   gated_attention_kernel  o = x * 2 sigmoid(gate_logit[token, head]) -> quant or bf16
+//                           (triton_ops.py:293-345)
+//   gelu_quant_kernel       o = x * sigmoid(1.702 x) -> quant  (triton_ops.py:98-126, USE_GELU)
+//
+// Layout: one warp per token row (H <= 32 * 8 * kChunks bf16).  Lane l owns the
+// 16-byte chunks c = 32 i + l; a 1x128 group is 16 consecutive chunks, so load i
+// of lanes 0-15 is group 2i and of lanes 16-31 group 2i+1, and a group's abs-max
+// is a 16-lane shuffle reduction.  Row sums of squares are reduced in a fixed
+// order (lane-sequential over its chunks, then an xor butterfly 16, 8, 4, 2, 1),
+// and every other step is an IEEE-rounded operation (1/sqrt is sqrt then a
+// division, e^x is built from fused multiply-adds), so the CPU oracle
+// reproduces the outputs bit for bit.
+#pragma once
+
+#include "quant.cuh"
+
+namespace ltxfp8 {
+
+constexpr int kProdWarps = 8;  // rows per 256-thread block
+
+// e^x from IEEE operations only: Cody-Waite argument reduction x = k ln2 + r
+// (ln2 split into a 15-bit head and a tail so k * head is exact), the Taylor
+// series of e^r to degree 7 in Horner form (|r| <= ln2/2, truncation < 2^-27
+// relative), and an exact two-step scaling by 2^k.  Deterministic on any IEEE
+// fp32 machine with a fused multiply-add; accurate to about 1 ulp.
+__device__ __forceinline__ float exp_cw(float x) {
+  if (x != x) return x;
+  if (x > 88.8f) return __int_as_float(0x7f800000);
+  if (x < -104.0f) return 0.0f;
+  const float k = rintf(__fmul_rn(x, 1.44269504088896341f));
+  float r = fmaf(-k, 0.693145751953125f, x);
+  r = fmaf(-k, 1.42860682030941723212e-6f, r);
+  float p = 1.98412698412698413e-4f;         // 1/7!
+  p = fmaf(p, r, 1.38888888888888889e-3f);  // 1/6!
+  p = fmaf(p, r, 8.33333333333333333e-3f);  // 1/5!
+  p = fmaf(p, r, 4.16666666666666667e-2f);  // 1/4!
+  p = fmaf(p, r, 1.66666666666666667e-1f);  // 1/3!
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int ki = static_cast<int>(k);
+  const int k1 = ki / 2, k2 = ki - k1;
+  p = __fmul_rn(p, __int_as_float((k1 + 127) << 23));
+  return __fmul_rn(p, __int_as_float((k2 + 127) << 23));
+}
+
+// 1 / (1 + e^-x) with an IEEE division.
+__device__ __forceinline__ float sigmoid_cw(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cw(-x))); }
+
+__device__ __forceinline__ float warp_sum_butterfly(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+// 1/sqrt as an IEEE square root followed by an IEEE division.
+__device__ __forceinline__ float rsqrt_ieee(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
+
+__device__ __forceinline__ float bf16_rn(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&f)[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+
+// 1x128 quantisation of the 8 values this lane holds of one group (the group's
+// other 120 values are in the 15 lanes sharing this half-warp): codes to q8
+// (8 bytes), the group's stored scale 1/s to *sfa by the half-warp's first lane.
+template <int kMode>
+__device__ __forceinline__ void quant_group8(const float (&f)[8], bool valid, uint8_t* q8, float* sfa_elem,
+                                             int l16) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = (kMode == kQuantTriton) ? fmaxf(amax, fabsf(f[i])) : fmax_nan(amax, fabsf(f[i]));
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, amax, off, 16);
+    amax = (kMode == kQuantTriton) ? fmaxf(amax, o) : fmax_nan(amax, o);
+  }
+  float s, inv;
+  group_scale<kMode>(amax, s, inv);
+  const bool in_range = (kMode == kQuantTriton) || isfinite(s);
+  uint32_t w[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float v0 = __fmul_rn(f[4 * i], s), v1 = __fmul_rn(f[4 * i + 1], s);
+    const float v2 = __fmul_rn(f[4 * i + 2], s), v3 = __fmul_rn(f[4 * i + 3], s);
+    const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+    const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
+    w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  }
+  if (valid) {
+    *reinterpret_cast<uint2*>(q8) = make_uint2(w[0], w[1]);
+    if (l16 == 0) *sfa_elem = inv;
+  }
+}
+
+// Sum over this lane's chunks of bf16(v*v), chunk by chunk, element by element.
+template <int kChunks>
+__device__ __forceinline__ float lane_sumsq_bf16(const uint4 (&v)[kChunks], int lane, int nchunks) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    if (i * 32 + lane < nchunks) {
+      float f[8];
+      bf16x8_to_f32(v[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, bf16_rn(__fmul_rn(f[j], f[j])));
+    }
+  }
+  return acc;
+}
+
+struct ProducerOut {
+  uint8_t* q;      // e4m3 [M, H] or null
+  float* sfa;      // sfa[kb * sfa_ld + m]
+  int64_t sfa_ld;
+  __nv_bfloat16* out;  // bf16 [M, H] (unquantised output) or null
+};
+
+// x bf16 [B*S, H]; scale/shift element (b, s, h) at p[b * bstride + s * sstride + h].
+template <int kChunks, int kMode>
+__global__ void __launch_bounds__(kProdWarps * 32) adanorm_quant_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t M, int64_t S, int H, const __nv_bfloat16* __restrict__ scale,
+    int64_t scale_bs, int64_t scale_ss, const __nv_bfloat16* __restrict__ shift, int64_t shift_bs, int64_t shift_ss,
+    ProducerOut o) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l16 = lane & 15;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kProdWarps + warp;
+  if (row >= M) return;
+  const int nchunks = H / 8;
+  const __nv_bfloat16* xr = x + row * H;
+  uint4 v[kChunks];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    v[i] = c < nchunks ? ldg16(xr + c * 8) : make_uint4(0, 0, 0, 0);
+  }
+  // mean of bf16 squares, + eps, 1/sqrt (triton_ops.py:82-85)
+  const float ss = warp_sum_butterfly(lane_sumsq_bf16<kChunks>(v, lane, nchunks));
+  const float r = rsqrt_ieee(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), 1e-5f));
+  const int64_t b = row / S, s = row - b * S;
+  const __nv_bfloat16* scr = scale + b * scale_bs + s * scale_ss;
+  const __nv_bfloat16* shr = shift + b * shift_bs + s * shift_ss;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    const bool valid = c < nchunks;
+    if (i * 32 >= nchunks) break;  // warp-uniform: no group of this load exists
+    float f[8], sc[8], sh[8];
+    bf16x8_to_f32(v[i], f);
+    bf16x8_to_f32(valid ? ldg16(scr + c * 8) : make_uint4(0, 0, 0, 0), sc);
+    bf16x8_to_f32(valid ? ldg16(shr + c * 8) : make_uint4(0, 0, 0, 0), sh);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float y = bf16_rn(__fmul_rn(f[j], r));           // (x * x_norm).to(bf16)
+      const float t = bf16_rn(__fadd_rn(1.0f, sc[j]));       // 1.0 + norm_scales (bf16)
+      f[j] = bf16_rn(__fadd_rn(bf16_rn(__fmul_rn(y, t)), sh[j]));  // x * t + shift, bf16 steps
+    }
+    quant_group8<kMode>(f, valid, o.q + row * H + c * 8, o.sfa + static_cast<int64_t>(c / 16) * o.sfa_ld + row, l16);
+  }
+}
+
+// x, y bf16 [B*S, H]; z (b, s, h) at z[b * bstride + s * sstride + h].
+// x <- bf16(x + bf16(y z)); o = x * rsqrt(mean(bf16(x^2))) in fp32; quantised
+// (o.q) or rounded to bf16 (o.out).
+template <int kChunks, int kMode, bool kQuant>
+__global__ void __launch_bounds__(kProdWarps * 32) rms_fma_kernel(__nv_bfloat16* __restrict__ x,
+                                                                const __nv_bfloat16* __restrict__ y, int64_t M,
+                                                                int64_t S, int H, const __nv_bfloat16* __restrict__ z,
+                                                                int64_t z_bs, int64_t z_ss, ProducerOut o) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l16 = lane & 15;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kProdWarps + warp;
+  if (row >= M) return;
+  const int nchunks = H / 8;
+  __nv_bfloat16* xr = x + row * H;
+  const __nv_bfloat16* yr = y + row * H;
+  const int64_t b = row / S, s = row - b * S;
+  const __nv_bfloat16* zr = z + b * z_bs + s * z_ss;
+  uint4 v[kChunks];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    if (c < nchunks) {
+      float fx[8], fy[8], fz[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(xr + c * 8), fx);
+      bf16x8_to_f32(ldg16(yr + c * 8), fy);
+      bf16x8_to_f32(ldg16(zr + c * 8), fz);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) fx[j] = bf16_rn(__fadd_rn(fx[j], bf16_rn(__fmul_rn(fy[j], fz[j]))));
+      v[i] = pack_bf16x8(fx);
+      *reinterpret_cast<uint4*>(xr + c * 8) = v[i];  // residual stream updated in place
+    } else {
+      v[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  const float ss = warp_sum_butterfly(lane_sumsq_bf16<kChunks>(v, lane, nchunks));
+  const float r = rsqrt_ieee(__fdiv_rn(ss, static_cast<float>(H)));  // no epsilon (triton_ops.py:222-224)
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    const bool valid = c < nchunks;
+    if (i * 32 >= nchunks) break;
+    float f[8];
+    bf16x8_to_f32(v[i], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = __fmul_rn(f[j], r);
+    if constexpr (kQuant) {
+      quant_group8<kMode>(f, valid, o.q + row * H + c * 8, o.sfa + static_cast<int64_t>(c / 16) * o.sfa_ld + row,
+                          l16);
+    } else {
+      if (valid) *reinterpret_cast<uint4*>(o.out + row * H + c * 8) = pack_bf16x8(f);
+    }
+  }
+}
+
+// x bf16 [M, H] viewed as [heads, H/heads]; gate_logits [M, heads] (bf16 or fp32);
+// o = x * 2 sigmoid(logit) in fp32, quantised or rounded to bf16.
+template <int kChunks, int kMode, bool kQuant, bool kGateF32>
+__global__ void __launch_bounds__(kProdWarps * 32) gated_attention_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                        const void* __restrict__ gate_logits,
+                                                                        int64_t M, int H, int heads, ProducerOut o) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l16 = lane & 15;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kProdWarps + warp;
+  if (row >= M) return;
+  const int nchunks = H / 8;
+  const int dim_head = H / heads;
+  const __nv_bfloat16* xr = x + row * H;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    const bool valid = c < nchunks;
+    if (i * 32 >= nchunks) break;
+    float f[8];
+    bf16x8_to_f32(valid ? ldg16(xr + c * 8) : make_uint4(0, 0, 0, 0), f);
+    // dim_head % 8 == 0: a chunk lies within one head
+    const int head = valid ? (c * 8) / dim_head : 0;
+    float g;
+    if constexpr (kGateF32) {
+      g = __ldg(static_cast<const float*>(gate_logits) + row * heads + head);
+    } else {
+      g = __bfloat162float(static_cast<const __nv_bfloat16*>(gate_logits)[row * heads + head]);
+    }
+    const float gate = __fmul_rn(2.0f, sigmoid_cw(g));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = __fmul_rn(f[j], gate);
+    if constexpr (kQuant) {
+      quant_group8<kMode>(f, valid, o.q + row * H + c * 8, o.sfa + static_cast<int64_t>(c / 16) * o.sfa_ld + row,
+                          l16);
+    } else {
+      if (valid) *reinterpret_cast<uint4*>(o.out + row * H + c * 8) = pack_bf16x8(f);
+    }
+  }
+}
+
+// x bf16 [M, K] (row stride x_ld) -> gelu(x) = x sigmoid(1.702 x) in fp32 -> quant.
+// Half-warp per 1x128 group as in quant_act_1x128_kernel.
+template <int kMode>
+__global__ void __launch_bounds__(256) gelu_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_ld, int64_t M,
+                                                         int64_t KB, uint8_t* __restrict__ q, int64_t q_ld,
+                                                         float* __restrict__ sfa, int64_t sfa_ld) {
+  const int t = threadIdx.x;
+  const int l16 = t & 15;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kQuantRowsPerBlock + (t >> 4);
+  const int64_t kb0 = static_cast<int64_t>(blockIdx.y) * kQuantGroupsPerThread;
+  const bool row_ok = row < M;
+  uint4 v[kQuantGroupsPerThread];
+#pragma unroll
+  for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+    const int64_t kb = kb0 + u;
+    v[u] = (row_ok && kb < KB) ? ldg16(x + row * x_ld + kb * 128 + l16 * 8) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+    const int64_t kb = kb0 + u;
+    float f[8];
+    bf16x8_to_f32(v[u], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = __fmul_rn(f[j], sigmoid_cw(__fmul_rn(1.702f, f[j])));
+    const bool valid = row_ok && kb < KB;
+    quant_group8<kMode>(f, valid, q + row * q_ld + kb * 128 + l16 * 8, sfa + kb * sfa_ld + row, l16);
+  }
+}
+
+}  // namespace ltxfp8

@@ -14,9 +14,13 @@ The activation quantiser's arithmetic is selectable (``set_quant_mode``):
 ``"torch"`` (default) is bit-exact with the reference's ``blockwise_quantize_torch``;
 ``"triton"`` reproduces the Triton kernel's division instruction.
 
-Names that belong to other parts of the reference (FP6 packing, the fused
-AdaLN / residual / gated-attention producers, RMSNorm+RoPE) are exported so the
-import list resolves, and raise ``NotImplementedError`` when called.
+* ``blockwise::adanorm``, ``blockwise::quant_rms_fma``, ``blockwise::rms_fma``,
+  ``blockwise::gated_attention`` and ``blockwise::quantize(use_gelu=True)`` -- the
+  fused producers of triton_ops.py:52-345 (csrc/producers.cuh).
+
+Names that belong to other parts of the reference (FP6 packing, RMSNorm+RoPE)
+are exported so the import list resolves, and raise ``NotImplementedError`` when
+called.
 """
 from __future__ import annotations
 
@@ -45,12 +49,12 @@ def get_quant_mode() -> str:
 
 @torch.library.custom_op("blockwise::quantize", mutates_args=())
 def _quant_blockwise(x: torch.Tensor, use_gelu: bool) -> Tuple[torch.Tensor, torch.Tensor]:
-    if use_gelu:
-        raise NotImplementedError(
-            "blockwise::quantize(use_gelu=True) applies x*sigmoid(1.702x) (triton_ops.py:98-100), which no "
-            "ltx-core caller uses; the FFN's GELU-tanh is fused into the GEMM epilogue instead")
     b, s, h = x.shape
-    q, sc = ops.quantize_1x128(x, _QUANT_MODE)
+    if use_gelu:
+        # x * sigmoid(1.702 x) before the quantiser (triton_ops.py:98-100,119-120)
+        q, sc = ops.gelu_quantize_1x128(x, _QUANT_MODE)
+    else:
+        q, sc = ops.quantize_1x128(x, _QUANT_MODE)
     return q.view(b, s, h), sc
 
 
@@ -77,7 +81,115 @@ def blockwise_quantize_triton(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tens
     return _quant_blockwise(x, False)
 
 
+def blockwise_quantize_gelu_triton(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``blockwise::quantize(x, True)``: quantise x * sigmoid(1.702 x) (triton_ops.py:156-157,441)."""
+    return _quant_blockwise(x, True)
+
+
 run_quant_blockwise_tma_aligned = blockwise_quantize_triton
+run_quant_blockwise_gelu_tma_aligned = blockwise_quantize_gelu_triton
+
+
+# ----------------------------------------------------------------------------- fused producers
+# Same op names, schemas and outputs as the reference's Triton producers
+# (triton_ops.py:158-345); arithmetic as documented in csrc/producers.cuh.
+def _scales_like(num_rows: int, h: int, device) -> torch.Tensor:
+    return ops.empty_act_scales(num_rows, h // 128, device)
+
+
+@torch.library.custom_op("blockwise::adanorm", mutates_args=())
+def _adanorm(x: torch.Tensor, w: Optional[torch.Tensor], norm_scale: torch.Tensor, norm_shift: torch.Tensor,
+             out_dtype: torch.dtype, hd_scale: Optional[float]) -> Tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm (eps 1e-5) -> bf16 -> x * (1 + norm_scale) + norm_shift -> 1x128 e4m3
+    (triton_ops.py:158-186).  ``w`` and ``hd_scale`` are accepted and unused, as in the
+    reference; the output is always e4m3."""
+    b, s, h = x.shape
+    q, sc = ops.adanorm_quantize(x, norm_scale, norm_shift, _QUANT_MODE)
+    return q.view(b, s, h), sc
+
+
+@_adanorm.register_fake
+def _adanorm_fake(x, w, norm_scale, norm_shift, out_dtype, hd_scale):
+    b, s, h = x.shape
+    return (torch.empty((b, s, h), dtype=torch.float8_e4m3fn, device=x.device), _scales_like(b * s, h, x.device))
+
+
+@torch.library.custom_op("blockwise::quant_rms_fma", mutates_args=("x",))
+def _quant_rms_fma(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """x += y * z in place, RMS-normalise, 1x128 e4m3 (triton_ops.py:234-262)."""
+    b, s, h = x.shape
+    q, sc = ops.rms_fma(x, y, z, True, _QUANT_MODE)
+    return q.view(b, s, h), sc
+
+
+@_quant_rms_fma.register_fake
+def _quant_rms_fma_fake(x, y, z):
+    b, s, h = x.shape
+    return (torch.empty((b, s, h), dtype=torch.float8_e4m3fn, device=x.device), _scales_like(b * s, h, x.device))
+
+
+@torch.library.custom_op("blockwise::rms_fma", mutates_args=("x",))
+def _rms_fma(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    """x += y * z in place, RMS-normalise, bf16 out (triton_ops.py:265-290)."""
+    b, s, h = x.shape
+    return ops.rms_fma(x, y, z, False, _QUANT_MODE).view(b, s, h)
+
+
+@_rms_fma.register_fake
+def _rms_fma_fake(x, y, z):
+    return torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+
+
+@torch.library.custom_op("blockwise::gated_attention", mutates_args=())
+def _gated_attention(x: torch.Tensor, gate_logits: torch.Tensor, quantize: bool = True
+                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """x * 2 sigmoid(gate_logits) per head, then 1x128 e4m3 (triton_ops.py:309-345).
+    With quantize=False the bf16 output comes with an empty scale tensor (a custom op
+    cannot return None; ``gated_attention_triton`` turns it into None like the reference)."""
+    b, t, h = x.shape
+    if quantize:
+        q, sc = ops.gated_attention(x, gate_logits, True, _QUANT_MODE)
+        return q.view(b, t, h), sc
+    out = ops.gated_attention(x, gate_logits, False, _QUANT_MODE)
+    return out.view(b, t, h), torch.empty(0, dtype=torch.float32, device=x.device)
+
+
+@_gated_attention.register_fake
+def _gated_attention_fake(x, gate_logits, quantize=True):
+    b, t, h = x.shape
+    if quantize:
+        return (torch.empty((b, t, h), dtype=torch.float8_e4m3fn, device=x.device), _scales_like(b * t, h, x.device))
+    return torch.empty((b, t, h), dtype=torch.bfloat16, device=x.device), torch.empty(0, device=x.device)
+
+
+def blockwise_quantize_adanorm_triton(x: torch.Tensor, w: Optional[torch.Tensor], norm_scale: torch.Tensor,
+                                      norm_shift: torch.Tensor, out_dtype: torch.dtype = torch.float8_e4m3fn,
+                                      hd_scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """triton_ops.py:438 (``run_quant_blockwise_norm_tma_aligned``)."""
+    return _adanorm(x, w, norm_scale, norm_shift, out_dtype, hd_scale)
+
+
+def blockwise_quantize_rms_fma_triton(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor
+                                      ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """triton_ops.py:442 (``run_quant_blockwise_rms_fma``); updates x in place."""
+    return _quant_rms_fma(x, y, z)
+
+
+def rms_fma_triton(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    """triton_ops.py:443 (``run_rms_fma``); updates x in place."""
+    return _rms_fma(x, y, z)
+
+
+def gated_attention_triton(x: torch.Tensor, gate_logits: torch.Tensor, quantize: bool = True):
+    """triton_ops.py:444 (``run_gated_attention``): (e4m3, scales), or (bf16, None)."""
+    out, sc = _gated_attention(x, gate_logits, quantize)
+    return (out, sc) if quantize else (out, None)
+
+
+run_quant_blockwise_norm_tma_aligned = blockwise_quantize_adanorm_triton
+run_quant_blockwise_rms_fma = blockwise_quantize_rms_fma_triton
+run_rms_fma = rms_fma_triton
+run_gated_attention = gated_attention_triton
 
 
 def blockwise_dequantize_triton(x: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
@@ -124,8 +236,5 @@ def _not_provided(name: str):
 fp6_blockwise_quantize_weights_torch = _not_provided("fp6_blockwise_quantize_weights_torch")
 fp6_pack_tensor = _not_provided("fp6_pack_tensor")
 fp6_unpack_tensor = _not_provided("fp6_unpack_tensor")
-blockwise_quantize_adanorm_triton = _not_provided("blockwise_quantize_adanorm_triton")
-blockwise_quantize_rms_fma_triton = _not_provided("blockwise_quantize_rms_fma_triton")
-gated_attention_triton = _not_provided("gated_attention_triton")
 rms_norm_rope = _not_provided("rms_norm_rope")
 rms_norm_split_rope = _not_provided("rms_norm_split_rope")

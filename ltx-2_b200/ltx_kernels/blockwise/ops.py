@@ -127,6 +127,116 @@ def dequantize_1x128(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return out
 
 
+# ----------------------------------------------------------------------------- fused producers
+def _rows3(x: torch.Tensor, name: str) -> Tuple[int, int, int]:
+    if x.dim() != 3:
+        raise RuntimeError(f"{name}: expected a [b, s, h] tensor, got shape {tuple(x.shape)}")
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: expected bf16, got {x.dtype}")
+    if not x.is_contiguous():
+        raise RuntimeError(f"{name}: x must be contiguous")
+    return x.shape[0], x.shape[1], x.shape[2]
+
+
+def _param3(p: torch.Tensor, b: int, s: int, h: int, name: str) -> Tuple[int, int]:
+    """(batch stride, token stride) of a [b, 1 or s, h] bf16 parameter; token stride 0
+    when it broadcasts over the sequence (triton_ops.py:161,213)."""
+    if p.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: expected bf16, got {p.dtype}")
+    if p.dim() != 3 or p.shape[0] != b or p.shape[1] not in (1, s) or p.shape[2] != h or p.stride(2) != 1:
+        raise RuntimeError(f"{name}: expected a [{b}, 1 or {s}, {h}] tensor with unit inner stride, "
+                           f"got shape {tuple(p.shape)} strides {p.stride()}")
+    return p.stride(0), (0 if p.shape[1] == 1 else p.stride(1))
+
+
+def adanorm_quantize(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                     mode: int = L.QUANT_TORCH) -> Tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm + AdaLN modulation + 1x128 quant: bf16 [b, s, h] -> (e4m3 [b*s, h], scales)."""
+    _require_cuda("adanorm_quantize", x, scale, shift)
+    b, s, h = _rows3(x, "adanorm_quantize")
+    # The reference decides broadcasting from norm_scale alone (triton_ops.py:161).
+    sc_bs, sc_ss = _param3(scale, b, s, h, "adanorm_quantize: scale")
+    sh_bs, sh_ss = _param3(shift, b, s, h, "adanorm_quantize: shift")
+    if sc_ss == 0:
+        sh_ss = 0
+    M = b * s
+    q = torch.empty((M, h), dtype=torch.float8_e4m3fn, device=x.device)
+    sfa = empty_act_scales(M, h // 128 if h % 128 == 0 else 0, x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_adanorm_quantize(x.data_ptr(), b, s, h, scale.data_ptr(), sc_bs, sc_ss,
+                                                  shift.data_ptr(), sh_bs, sh_ss, q.data_ptr(), sfa.data_ptr(),
+                                                  align4(M), mode, _stream(x)))
+    return q, sfa
+
+
+def rms_fma(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor, quantize: bool = True,
+            mode: int = L.QUANT_TORCH):
+    """x <- x + y * z (in place), then RMS-normalise; returns (e4m3 [b*s, h], scales) or bf16 [b*s, h]."""
+    _require_cuda("rms_fma", x, y, z)
+    b, s, h = _rows3(x, "rms_fma")
+    if y.shape != x.shape or y.dtype != torch.bfloat16 or not y.is_contiguous():
+        raise RuntimeError("rms_fma: y must be a contiguous bf16 tensor shaped like x")
+    z_bs, z_ss = _param3(z, b, s, h, "rms_fma: z")
+    M = b * s
+    q = sfa = out = None
+    if quantize:
+        q = torch.empty((M, h), dtype=torch.float8_e4m3fn, device=x.device)
+        sfa = empty_act_scales(M, h // 128 if h % 128 == 0 else 0, x.device)
+    else:
+        out = torch.empty((M, h), dtype=torch.bfloat16, device=x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_rms_fma(x.data_ptr(), y.data_ptr(), b, s, h, z.data_ptr(), z_bs, z_ss,
+                                         None if q is None else q.data_ptr(),
+                                         None if sfa is None else sfa.data_ptr(), align4(M),
+                                         None if out is None else out.data_ptr(), mode, _stream(x)))
+    return (q, sfa) if quantize else out
+
+
+def gated_attention(x: torch.Tensor, gate_logits: torch.Tensor, quantize: bool = True,
+                    mode: int = L.QUANT_TORCH):
+    """x bf16 [b, t, h] * 2 sigmoid(gate_logits [b, t, heads]) per head; quantised or bf16 [b*t, h]."""
+    _require_cuda("gated_attention", x, gate_logits)
+    b, t, h = _rows3(x, "gated_attention")
+    heads = gate_logits.shape[-1]
+    if gate_logits.shape[:-1] != x.shape[:-1]:
+        raise RuntimeError(f"gated_attention: gate_logits shape {tuple(gate_logits.shape)} does not match x")
+    gdt = {torch.bfloat16: L.DTYPE_BF16, torch.float32: L.DTYPE_F32}.get(gate_logits.dtype)
+    if gdt is None:
+        raise RuntimeError(f"gated_attention: gate logits must be bf16 or fp32, got {gate_logits.dtype}")
+    g = gate_logits.contiguous()
+    M = b * t
+    q = sfa = out = None
+    if quantize:
+        q = torch.empty((M, h), dtype=torch.float8_e4m3fn, device=x.device)
+        sfa = empty_act_scales(M, h // 128 if h % 128 == 0 else 0, x.device)
+    else:
+        out = torch.empty((M, h), dtype=torch.bfloat16, device=x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_gated_attention(x.data_ptr(), g.data_ptr(), gdt, M, h, heads,
+                                                 None if q is None else q.data_ptr(),
+                                                 None if sfa is None else sfa.data_ptr(), align4(M),
+                                                 None if out is None else out.data_ptr(), mode, _stream(x)))
+    return (q, sfa) if quantize else out
+
+
+def gelu_quantize_1x128(x: torch.Tensor, mode: int = L.QUANT_TORCH) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [..., K] -> 1x128 quant of x * sigmoid(1.702 x): (e4m3 [M, K], scales)."""
+    _require_cuda("gelu_quantize_1x128", x)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"gelu_quantize_1x128 expects bf16 input, got {x.dtype}")
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    s = empty_act_scales(M, K // 128 if K % 128 == 0 else 0, x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_gelu_quantize_1x128(x2.data_ptr(), M, K, x2.stride(0), q.data_ptr(), K,
+                                                     s.data_ptr(), align4(M), mode, _stream(x)))
+    return q, s
+
+
 # ----------------------------------------------------------------------------- GEMM
 def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Tensor,
          bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,

@@ -25,6 +25,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #if defined(__FLT_EVAL_METHOD__) && __FLT_EVAL_METHOD__ != 0
@@ -233,4 +234,224 @@ void orc_f32_to_e4m3_array(const float* f, int64_t n, uint8_t* out) {
 
 void orc_f32_to_bf16_array(const float* f, int64_t n, uint16_t* out) {
     for (int64_t i = 0; i < n; ++i) out[i] = orc_f32_to_bf16(f[i]);
+}
+
+/* ------------------------------------------------------------------------
+ * Fused producers (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:52-96,
+ * 98-126, 188-290, 293-345).  Parity unpinned: the reference runs these as
+ * Triton GPU kernels, which cannot execute in this container, and its tests
+ * hold no fixtures for them.  The restatement keeps the reference's dtype
+ * semantics (Triton promotion rules: bf16 op bf16 -> bf16, bf16 op fp32 -> fp32,
+ * a Python float scalar takes the tensor's dtype) and fixes the arithmetic the
+ * reference leaves to the compiler:
+ *   - row sums of bf16(x^2) accumulate in fp32 in the CUDA kernels' order:
+ *     per lane l of 32, its 16-byte chunks c = 32 i + l (8 values each) in order,
+ *     then an xor butterfly over the lanes with offsets 16, 8, 4, 2, 1
+ *     (the reference reduces in bf16 in Triton's layout order);
+ *   - 1/sqrt(v) = RN(1 / RN(sqrt(v))) (the reference: rsqrt approximation);
+ *   - e^x by Cody-Waite reduction and the degree-7 Taylor series (exp_cw below),
+ *     1/(1+e) by IEEE division (the reference: fast exp and division);
+ *   - quantisation in the torch arithmetic of orc_quant_act_1x128 on fp32 inputs.
+ * -------------------------------------------------------------------- */
+
+static float rn_bf16(float v) { return orc_bf16_to_f32(orc_f32_to_bf16(v)); }
+
+/* e^x: x = k ln2 + r with ln2 = 0.693145751953125 (15 significant bits, so k*head
+   is exact) + 1.42860682030941723212e-6; e^r by Taylor to degree 7 (Horner, fma);
+   scale by 2^k in two exact halves. */
+static float exp_cw(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    volatile float t = x * 1.44269504088896341f;
+    float k = rintf(t);
+    float r = fmaf(-k, 0.693145751953125f, x);
+    r = fmaf(-k, 1.42860682030941723212e-6f, r);
+    float p = 1.98412698412698413e-4f;
+    p = fmaf(p, r, 1.38888888888888889e-3f);
+    p = fmaf(p, r, 8.33333333333333333e-3f);
+    p = fmaf(p, r, 4.16666666666666667e-2f);
+    p = fmaf(p, r, 1.66666666666666667e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ki = (int)k;
+    int k1 = ki / 2, k2 = ki - k1;
+    volatile float a = p * f32_from_bits((uint32_t)(k1 + 127) << 23);
+    volatile float b = a * f32_from_bits((uint32_t)(k2 + 127) << 23);
+    return b;
+}
+
+float orc_exp_cw(float x) { return exp_cw(x); }
+
+static float sigmoid_cw(float x) {
+    volatile float e = exp_cw(-x);
+    volatile float d = 1.0f + e;
+    volatile float s = 1.0f / d;
+    return s;
+}
+
+static float rsqrt_ieee(float v) {
+    volatile float sq = sqrtf(v);
+    volatile float r = 1.0f / sq;
+    return r;
+}
+
+/* Sum of bf16(x^2) over a row of H bf16 values in the kernels' lane/butterfly order. */
+static float row_sumsq_bf16(const float* x, int64_t H) {
+    float part[32];
+    int64_t nchunks = H / 8;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int64_t c = l; c < nchunks; c += 32)
+            for (int j = 0; j < 8; ++j) {
+                volatile float sq = x[c * 8 + j] * x[c * 8 + j];
+                volatile float s = acc + rn_bf16(sq);
+                acc = s;
+            }
+        part[l] = acc;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        float nxt[32];
+        for (int l = 0; l < 32; ++l) {
+            volatile float s = part[l] + part[l ^ off];
+            nxt[l] = s;
+        }
+        memcpy(part, nxt, sizeof(part));
+    }
+    return part[0];
+}
+
+/* Torch-arithmetic 1x128 quantisation of one row of fp32 values. */
+static void quant_row_f32(const float* v, int64_t H, int64_t m, uint8_t* q, float* sfa, int64_t sfa_ld) {
+    for (int64_t kb = 0; kb < H / 128; ++kb) {
+        const float* g = v + kb * 128;
+        float amax = 0.0f;
+        for (int i = 0; i < 128; ++i) amax = amax_nan(amax, fabsf(g[i]));
+        volatile float r = 1.0f / amax;
+        volatile float s = r * 448.0f;
+        for (int i = 0; i < 128; ++i) {
+            volatile float t = g[i] * s;
+            q[m * H + kb * 128 + i] = orc_f32_to_e4m3(t);
+        }
+        volatile float inv = 1.0f / s;
+        sfa[kb * sfa_ld + m] = inv;
+    }
+}
+
+/*
+ * AdaLN producer, _block_quant_norm_kernel (triton_ops.py:52-96):
+ *   x_norm = sum(bf16(x*x)) / H; r = rsqrt(x_norm + 1e-5)        (:82-84)
+ *   y = bf16(x * r)                                               (:85, bf16 * fp32 -> fp32)
+ *   z = bf16(bf16(y * bf16(1 + scale)) + shift)                   (:86, bf16 arithmetic)
+ *   (q, sfa) = quant(z)                                           (:88-92)
+ * scale/shift of (b, s) at p[b * bs + s * ss] (ss = 0 broadcasts, :74-80).
+ */
+void orc_adanorm_quant(const uint16_t* x, int64_t B, int64_t S, int64_t H,
+                       const uint16_t* scale, int64_t sc_bs, int64_t sc_ss,
+                       const uint16_t* shift, int64_t sh_bs, int64_t sh_ss,
+                       uint8_t* q, float* sfa, int64_t sfa_ld) {
+    float* row = (float*)malloc(sizeof(float) * (size_t)H);
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t s = 0; s < S; ++s) {
+            int64_t m = b * S + s;
+            for (int64_t h = 0; h < H; ++h) row[h] = orc_bf16_to_f32(x[m * H + h]);
+            float ss = row_sumsq_bf16(row, H);
+            volatile float mean = ss / (float)H;
+            volatile float me = mean + 1e-5f;
+            float r = rsqrt_ieee(me);
+            const uint16_t* sc = scale + b * sc_bs + s * sc_ss;
+            const uint16_t* sh = shift + b * sh_bs + s * sh_ss;
+            for (int64_t h = 0; h < H; ++h) {
+                volatile float xy = row[h] * r;
+                float y = rn_bf16(xy);
+                volatile float tt = 1.0f + orc_bf16_to_f32(sc[h]);
+                float t = rn_bf16(tt);
+                volatile float u = y * t;
+                volatile float z = rn_bf16(u) + orc_bf16_to_f32(sh[h]);
+                row[h] = rn_bf16(z);
+            }
+            quant_row_f32(row, H, m, q, sfa, sfa_ld);
+        }
+    free(row);
+}
+
+/*
+ * Residual FMA + RMS, _quant_rms_sum_mult_kernel (triton_ops.py:188-232):
+ *   o = bf16(x + bf16(y * z)); x <- o                              (:209-211, bf16 arithmetic)
+ *   r = rsqrt(sum(bf16(o*o)) / H)                                  (:213-215, no epsilon)
+ *   v = o * r (fp32)                                               (:216)
+ *   QUANTIZE: (q, sfa) = quant(v) (:218-223); else out = bf16(v)   (:225-226)
+ * x is updated in place; q == NULL selects the bf16 output.
+ */
+void orc_rms_fma(uint16_t* x, const uint16_t* y, int64_t B, int64_t S, int64_t H,
+                 const uint16_t* z, int64_t z_bs, int64_t z_ss,
+                 uint8_t* q, float* sfa, int64_t sfa_ld, uint16_t* out) {
+    float* row = (float*)malloc(sizeof(float) * (size_t)H);
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t s = 0; s < S; ++s) {
+            int64_t m = b * S + s;
+            const uint16_t* zr = z + b * z_bs + s * z_ss;
+            for (int64_t h = 0; h < H; ++h) {
+                volatile float yz = orc_bf16_to_f32(y[m * H + h]) * orc_bf16_to_f32(zr[h]);
+                volatile float o = orc_bf16_to_f32(x[m * H + h]) + rn_bf16(yz);
+                uint16_t ob = orc_f32_to_bf16(o);
+                x[m * H + h] = ob;
+                row[h] = orc_bf16_to_f32(ob);
+            }
+            float ss = row_sumsq_bf16(row, H);
+            volatile float mean = ss / (float)H;
+            float r = rsqrt_ieee(mean);
+            for (int64_t h = 0; h < H; ++h) {
+                volatile float v = row[h] * r;
+                row[h] = v;
+            }
+            if (q) quant_row_f32(row, H, m, q, sfa, sfa_ld);
+            else for (int64_t h = 0; h < H; ++h) out[m * H + h] = orc_f32_to_bf16(row[h]);
+        }
+    free(row);
+}
+
+/*
+ * Gated attention, _gated_attention_kernel (triton_ops.py:271-306):
+ *   gate = 2 * sigmoid(float(logit[m, head]))   (:287-289)
+ *   v = float(x) * gate                          (:293-297)
+ *   QUANTIZE: quant(v) (:299-304); else out = bf16(v) (:305-306)
+ * logits: bf16 bit patterns (gate_f32 = 0) or fp32 (gate_f32 = 1), [M, heads].
+ */
+void orc_gated_attention(const uint16_t* x, const void* logits, int gate_f32, int64_t M, int64_t H,
+                         int64_t heads, uint8_t* q, float* sfa, int64_t sfa_ld, uint16_t* out) {
+    float* row = (float*)malloc(sizeof(float) * (size_t)H);
+    int64_t dh = H / heads;
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t h = 0; h < H; ++h) {
+            int64_t hd = h / dh;
+            float g = gate_f32 ? ((const float*)logits)[m * heads + hd]
+                               : orc_bf16_to_f32(((const uint16_t*)logits)[m * heads + hd]);
+            volatile float gate = 2.0f * sigmoid_cw(g);
+            volatile float v = orc_bf16_to_f32(x[m * H + h]) * gate;
+            row[h] = v;
+        }
+        if (q) quant_row_f32(row, H, m, q, sfa, sfa_ld);
+        else for (int64_t h = 0; h < H; ++h) out[m * H + h] = orc_f32_to_bf16(row[h]);
+    }
+    free(row);
+}
+
+/*
+ * GELU (sigmoid form) + quant, _block_quant_kernel with USE_GELU (triton_ops.py:98-126):
+ *   v = x * sigmoid(1.702 * x) in fp32 (:98-100,119-120); (q, sfa) = quant(v).
+ */
+void orc_gelu_quant(const uint16_t* x, int64_t M, int64_t K, uint8_t* q, float* sfa, int64_t sfa_ld) {
+    float* row = (float*)malloc(sizeof(float) * (size_t)K);
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t k = 0; k < K; ++k) {
+            float xv = orc_bf16_to_f32(x[m * K + k]);
+            volatile float t = 1.702f * xv;
+            volatile float v = xv * sigmoid_cw(t);
+            row[k] = v;
+        }
+        quant_row_f32(row, K, m, q, sfa, sfa_ld);
+    }
+    free(row);
 }

@@ -59,6 +59,12 @@ def lib():
         L.orc_e4m3_to_f32_array.argtypes = [vp, i64, vp]
         L.orc_f32_to_e4m3_array.argtypes = [vp, i64, vp]
         L.orc_f32_to_bf16_array.argtypes = [vp, i64, vp]
+        L.orc_adanorm_quant.argtypes = [vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp, vp, i64]
+        L.orc_rms_fma.argtypes = [vp, vp, i64, i64, i64, vp, i64, i64, vp, vp, i64, vp]
+        L.orc_gated_attention.argtypes = [vp, vp, i32, i64, i64, i64, vp, vp, i64, vp]
+        L.orc_gelu_quant.argtypes = [vp, i64, i64, vp, vp, i64]
+        L.orc_exp_cw.argtypes = [f32]
+        L.orc_exp_cw.restype = f32
         _lib = L
     return _lib
 
@@ -152,6 +158,86 @@ def gelu_tanh_bf16(x_bf16: np.ndarray) -> np.ndarray:
     y = np.empty_like(x)
     lib().orc_gelu_tanh_bf16_array(_p(x), x.size, _p(y))
     return y
+
+
+# ----------------------------------------------------------------------------- fused producers
+# Restatements of the reference's Triton producers (triton_ops.py:52-345) with the
+# arithmetic the CUDA kernels fix (fp32 row sums in lane/butterfly order, IEEE
+# sqrt + division, Cody-Waite exp).  Parity against the reference is unpinned:
+# its Triton kernels cannot run here.  All inputs are bf16 bit patterns (uint16).
+def _u16(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def _param_strides(p: np.ndarray, S: int):
+    """(buffer, bstride, sstride) of a [B, 1 or S, H] parameter (sstride 0 broadcasts)."""
+    B, T, H = p.shape
+    return _u16(p), T * H, (0 if T == 1 else H)
+
+
+def adanorm_quant(x: np.ndarray, scale: np.ndarray, shift: np.ndarray, sfa_ld: int | None = None):
+    """x [B, S, H], scale/shift [B, 1 or S, H] -> (codes [B*S, H], scales [H/128, ld])."""
+    x = _u16(x)
+    B, S, H = x.shape
+    M = B * S
+    ld = align4(M) if sfa_ld is None else sfa_ld
+    sc, sc_bs, sc_ss = _param_strides(scale, S)
+    sh, sh_bs, sh_ss = _param_strides(shift, S)
+    q = np.empty((M, H), np.uint8)
+    sfa = np.full((H // 128, ld), np.nan, np.float32)
+    lib().orc_adanorm_quant(_p(x), B, S, H, _p(sc), sc_bs, sc_ss, _p(sh), sh_bs, sh_ss, _p(q), _p(sfa), ld)
+    return q, sfa
+
+
+def rms_fma(x: np.ndarray, y: np.ndarray, z: np.ndarray, quantize: bool = True, sfa_ld: int | None = None):
+    """x, y [B, S, H], z [B, 1 or S, H] -> (updated x, codes, scales) or (updated x, bf16 out)."""
+    x = _u16(x).copy()
+    y = _u16(y)
+    B, S, H = x.shape
+    M = B * S
+    zb, z_bs, z_ss = _param_strides(z, S)
+    if quantize:
+        ld = align4(M) if sfa_ld is None else sfa_ld
+        q = np.empty((M, H), np.uint8)
+        sfa = np.full((H // 128, ld), np.nan, np.float32)
+        lib().orc_rms_fma(_p(x), _p(y), B, S, H, _p(zb), z_bs, z_ss, _p(q), _p(sfa), ld, None)
+        return x, q, sfa
+    out = np.empty((M, H), np.uint16)
+    lib().orc_rms_fma(_p(x), _p(y), B, S, H, _p(zb), z_bs, z_ss, None, None, 0, _p(out))
+    return x, out
+
+
+def gated_attention(x: np.ndarray, logits: np.ndarray, quantize: bool = True, sfa_ld: int | None = None):
+    """x [M, H] bf16 bits; logits [M, heads] bf16 bits (uint16) or float32."""
+    x = _u16(x)
+    M, H = x.shape
+    heads = logits.shape[-1]
+    f32 = logits.dtype == np.float32
+    lg = np.ascontiguousarray(logits, dtype=np.float32 if f32 else np.uint16)
+    if quantize:
+        ld = align4(M) if sfa_ld is None else sfa_ld
+        q = np.empty((M, H), np.uint8)
+        sfa = np.full((H // 128, ld), np.nan, np.float32)
+        lib().orc_gated_attention(_p(x), _p(lg), int(f32), M, H, heads, _p(q), _p(sfa), ld, None)
+        return q, sfa
+    out = np.empty((M, H), np.uint16)
+    lib().orc_gated_attention(_p(x), _p(lg), int(f32), M, H, heads, None, None, 0, _p(out))
+    return out
+
+
+def gelu_quant(x: np.ndarray, sfa_ld: int | None = None):
+    """x [M, K] bf16 bits -> 1x128 quant of x * sigmoid(1.702 x)."""
+    x = _u16(x)
+    M, K = x.shape
+    ld = align4(M) if sfa_ld is None else sfa_ld
+    q = np.empty((M, K), np.uint8)
+    sfa = np.full((K // 128, ld), np.nan, np.float32)
+    lib().orc_gelu_quant(_p(x), M, K, _p(q), _p(sfa), ld)
+    return q, sfa
+
+
+def exp_cw(x: float) -> float:
+    return float(lib().orc_exp_cw(x))
 
 
 # ----------------------------------------------------------------------------- GEMM oracles

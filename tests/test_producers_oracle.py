@@ -1,0 +1,113 @@
+"""CPU checks of the producer restatements in the oracle (no GPU).
+
+The reference's producers are Triton GPU kernels (triton_ops.py:52-345) that cannot
+run in this container, so parity against them is unpinned.  These tests check that
+the restatement computes the reference's formulas: its outputs are compared with
+float64 evaluations of the same expressions, within the precision of the output
+format (bf16, or e4m3 codes with 1x128 scales).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import activations, bits
+from oracle import oracle as O
+
+E4M3_REL = 4e-2   # relative Frobenius error of a 1x128 e4m3 round trip on these inputs
+BF16_REL = 5e-3   # relative Frobenius error of bf16 rounding
+
+
+def _f64(bf16_bits):
+    return O.bf16_to_f32(bf16_bits).astype(np.float64)
+
+
+def _param(b, t, h, seed, std=0.1):
+    g = torch.Generator().manual_seed(seed)
+    return bits((torch.randn(b, t, h, generator=g) * std).to(torch.bfloat16))
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def _dequant(q, sfa, M, H):
+    return O.dequant_act_f32(q, sfa[:, :M]).astype(np.float64).reshape(M, H)
+
+
+def test_exp_cw_within_one_ulp():
+    xs = np.concatenate([np.linspace(-87.0, 88.0, 4001), np.random.default_rng(0).normal(0, 4, 4000)])
+    for x in xs.astype(np.float32):
+        e, r = O.exp_cw(float(x)), math.exp(float(x))
+        assert abs(e - r) <= np.spacing(np.float32(r)), (x, e, r)
+    assert O.exp_cw(100.0) == math.inf and O.exp_cw(-120.0) == 0.0
+
+
+def test_adanorm_restatement_follows_formula():
+    B, S, H = 2, 16, 2048
+    x = bits(activations(B * S, H, seed=1)).reshape(B, S, H)
+    sc, sh = _param(B, 1, H, 2), _param(B, 1, H, 3)
+    q, sfa = O.adanorm_quant(x, sc, sh)
+    xf = _f64(x).reshape(B, S, H)
+    y = xf / np.sqrt((xf * xf).mean(-1, keepdims=True) + 1e-5)
+    z = y * (1.0 + _f64(sc)) + _f64(sh)
+    assert _rel(_dequant(q, sfa, B * S, H), z.reshape(B * S, H)) < E4M3_REL
+
+
+def test_rms_fma_restatement_follows_formula():
+    B, S, H = 1, 24, 4096
+    x = bits(activations(B * S, H, seed=4)).reshape(B, S, H)
+    y = bits(activations(B * S, H, seed=5)).reshape(B, S, H)
+    z = _param(B, S, H, 6, std=0.5)
+    xn, out = O.rms_fma(x, y, z, quantize=False)
+    o = _f64(x) + _f64(y) * _f64(z)
+    assert _rel(_f64(xn), o) < BF16_REL
+    ref = o / np.sqrt((o * o).mean(-1, keepdims=True))
+    assert _rel(_f64(out).reshape(B, S, H), ref) < BF16_REL
+    _, q, sfa = O.rms_fma(x, y, z, quantize=True)
+    assert _rel(_dequant(q, sfa, B * S, H), ref.reshape(B * S, H)) < E4M3_REL
+
+
+def test_gated_attention_restatement_follows_formula():
+    M, H, heads = 40, 2048, 32
+    x = bits(activations(M, H, seed=7))
+    g = np.random.default_rng(8).normal(0, 3, (M, heads)).astype(np.float32)
+    out = O.gated_attention(x, g, quantize=False)
+    gate = 2.0 / (1.0 + np.exp(-g.astype(np.float64)))
+    ref = _f64(x) * np.repeat(gate, H // heads, axis=1)
+    assert _rel(_f64(out), ref) < BF16_REL
+    q, sfa = O.gated_attention(x, g, quantize=True)
+    assert _rel(_dequant(q, sfa, M, H), ref) < E4M3_REL
+
+
+def test_gelu_quant_restatement_follows_formula():
+    M, K = 32, 1024
+    x = bits(activations(M, K, seed=9))
+    q, sfa = O.gelu_quant(x)
+    xf = _f64(x)
+    ref = xf / (1.0 + np.exp(-1.702 * xf))
+    assert _rel(_dequant(q, sfa, M, K), ref) < E4M3_REL
+
+
+@pytest.mark.parametrize("H", [100, 8320, 0])
+def test_producers_reject_bad_rows_without_device(H):
+    from ltx_kernels import _lib
+    L = _lib.load()
+    rc = L.ltxfp8_adanorm_quantize(16, 1, 4, H, 16, 0, 0, 16, 0, 0, 16, 16, 4, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED_SHAPE
+    rc = L.ltxfp8_rms_fma(16, 16, 1, 4, H, 16, 0, 0, 16, 16, 4, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED_SHAPE
+    rc = L.ltxfp8_gated_attention(16, 16, _lib.DTYPE_BF16, 4, H, 1, 16, 16, 4, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED_SHAPE
+
+
+def test_gated_attention_rejects_bad_heads_without_device():
+    from ltx_kernels import _lib
+    L = _lib.load()
+    rc = L.ltxfp8_gated_attention(16, 16, _lib.DTYPE_BF16, 4, 2048, 3, 16, 16, 4, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED_SHAPE
+    rc = L.ltxfp8_gated_attention(16, 16, _lib.DTYPE_BF16, 4, 2048, 512, 16, 16, 4, None, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED_SHAPE  # dim_head 4 is not a multiple of 8

@@ -59,8 +59,8 @@ def test_quant_op_and_torch_variant(cuda_device):
     assert q.shape == (2, 17, 512) and s.shape == (34, 4)
     assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
     assert torch.equal(s.t(), s2)
-    with pytest.raises(NotImplementedError):
-        torch.ops.blockwise.quantize(x, True)
+    qg, sg = torch.ops.blockwise.quantize(x, True)  # GELU (sigmoid form) before the quantiser
+    assert qg.shape == (2, 17, 512) and not torch.equal(qg.view(torch.uint8), q.view(torch.uint8))
 
 
 def test_quant_triton_mode_close(cuda_device):
