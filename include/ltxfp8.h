@@ -114,7 +114,7 @@ int ltxfp8_rms_fma(void* x, const void* y, int64_t B, int64_t S, int64_t H, cons
 /*
  * Gated attention output: o = x * 2 sigmoid(gate_logits[m, h / (H / heads)]) in fp32,
  * x bf16 [M, H], gate_logits [M, heads] of gate_dtype (LTXFP8_DTYPE_BF16 or _F32),
- * (H / heads) % 8 == 0.  With q != NULL the 1x128 quant of o, otherwise out = bf16(o).
+ * heads <= 64, (H / heads) % 8 == 0.  With q != NULL the 1x128 quant of o, otherwise out = bf16(o).
  * Replaces blockwise::gated_attention / gated_attention_triton (triton_ops.py:293-345).
  */
 int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtype, int64_t M, int64_t H,

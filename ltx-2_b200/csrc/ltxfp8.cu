@@ -285,25 +285,33 @@ int producer_out(const char* name, int64_t M, void* q, float* sfa, int64_t sfa_l
 }
 
 template <int kChunks, int kMode>
-void adanorm_launch(dim3 grid, cudaStream_t s, const __nv_bfloat16* x, int64_t M, int64_t S, int H,
-                    const __nv_bfloat16* sc, int64_t sc_bs, int64_t sc_ss, const __nv_bfloat16* sh, int64_t sh_bs,
-                    int64_t sh_ss, ProducerOut o) {
+cudaError_t adanorm_launch(const DeviceInfo* d, cudaStream_t s, const __nv_bfloat16* x, int64_t M, int64_t S, int H,
+                           const __nv_bfloat16* sc, int64_t sc_bs, int64_t sc_ss, const __nv_bfloat16* sh,
+                           int64_t sh_bs, int64_t sh_ss, ProducerOut o) {
+  (void)d;
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
   adanorm_quant_kernel<kChunks, kMode><<<grid, kProdWarps * 32, 0, s>>>(x, M, S, H, sc, sc_bs, sc_ss, sh, sh_bs,
                                                                         sh_ss, o);
+  return cudaGetLastError();
 }
 
 template <int kChunks, int kMode>
-void rms_fma_launch(dim3 grid, cudaStream_t s, __nv_bfloat16* x, const __nv_bfloat16* y, int64_t M, int64_t S, int H,
-                    const __nv_bfloat16* z, int64_t z_bs, int64_t z_ss, ProducerOut o) {
+cudaError_t rms_fma_launch(const DeviceInfo* d, cudaStream_t s, __nv_bfloat16* x, const __nv_bfloat16* y, int64_t M,
+                           int64_t S, int H, const __nv_bfloat16* z, int64_t z_bs, int64_t z_ss, ProducerOut o) {
+  (void)d;
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
   if (o.q)
     rms_fma_kernel<kChunks, kMode, true><<<grid, kProdWarps * 32, 0, s>>>(x, y, M, S, H, z, z_bs, z_ss, o);
   else
     rms_fma_kernel<kChunks, kMode, false><<<grid, kProdWarps * 32, 0, s>>>(x, y, M, S, H, z, z_bs, z_ss, o);
+  return cudaGetLastError();
 }
 
 template <int kChunks, int kMode>
-void gated_launch(dim3 grid, cudaStream_t s, const __nv_bfloat16* x, const void* g, bool g_f32, int64_t M, int H,
-                  int heads, ProducerOut o) {
+cudaError_t gated_launch(const DeviceInfo* d, cudaStream_t s, const __nv_bfloat16* x, const void* g, bool g_f32,
+                         int64_t M, int H, int heads, ProducerOut o) {
+  (void)d;
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
   if (o.q) {
     if (g_f32) gated_attention_kernel<kChunks, kMode, true, true><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
     else gated_attention_kernel<kChunks, kMode, true, false><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
@@ -311,18 +319,19 @@ void gated_launch(dim3 grid, cudaStream_t s, const __nv_bfloat16* x, const void*
     if (g_f32) gated_attention_kernel<kChunks, kMode, false, true><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
     else gated_attention_kernel<kChunks, kMode, false, false><<<grid, kProdWarps * 32, 0, s>>>(x, g, M, H, heads, o);
   }
+  return cudaGetLastError();
 }
 
-// Calls fn<kChunks, kMode>(args...) for the row length's chunk count and the mode.
-#define LTXFP8_PRODUCER_DISPATCH(fn, chunks, mode, ...)                        \
-  do {                                                                         \
-    const bool tri_ = (mode) == LTXFP8_QUANT_TRITON;                           \
-    switch (chunks) {                                                          \
-      case 4: tri_ ? fn<4, kQuantTriton>(__VA_ARGS__) : fn<4, kQuantTorch>(__VA_ARGS__); break;     \
-      case 8: tri_ ? fn<8, kQuantTriton>(__VA_ARGS__) : fn<8, kQuantTorch>(__VA_ARGS__); break;     \
-      case 16: tri_ ? fn<16, kQuantTriton>(__VA_ARGS__) : fn<16, kQuantTorch>(__VA_ARGS__); break;  \
-      default: tri_ ? fn<32, kQuantTriton>(__VA_ARGS__) : fn<32, kQuantTorch>(__VA_ARGS__); break;  \
-    }                                                                          \
+// err = fn<kChunks, kMode>(args...) for the row length's chunk count and the mode.
+#define LTXFP8_PRODUCER_DISPATCH(err, fn, chunks, mode, ...)                                        \
+  do {                                                                                             \
+    const bool tri_ = (mode) == LTXFP8_QUANT_TRITON;                                               \
+    switch (chunks) {                                                                              \
+      case 4: err = tri_ ? fn<4, kQuantTriton>(__VA_ARGS__) : fn<4, kQuantTorch>(__VA_ARGS__); break;     \
+      case 8: err = tri_ ? fn<8, kQuantTriton>(__VA_ARGS__) : fn<8, kQuantTorch>(__VA_ARGS__); break;     \
+      case 16: err = tri_ ? fn<16, kQuantTriton>(__VA_ARGS__) : fn<16, kQuantTorch>(__VA_ARGS__); break;  \
+      default: err = tri_ ? fn<32, kQuantTriton>(__VA_ARGS__) : fn<32, kQuantTorch>(__VA_ARGS__); break;  \
+    }                                                                                              \
   } while (0)
 
 }  // namespace
@@ -419,12 +428,11 @@ int ltxfp8_adanorm_quantize(const void* x, int64_t B, int64_t S, int64_t H, cons
   DeviceInfo* d;
   rc = device_info(&d);
   if (rc) return rc;
-  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
-  LTXFP8_PRODUCER_DISPATCH(adanorm_launch, producer_chunks(H), flags, grid, static_cast<cudaStream_t>(stream),
+  cudaError_t e = cudaSuccess;
+  LTXFP8_PRODUCER_DISPATCH(e, adanorm_launch, producer_chunks(H), flags, d, static_cast<cudaStream_t>(stream),
                            static_cast<const __nv_bfloat16*>(x), M, S, static_cast<int>(H),
                            static_cast<const __nv_bfloat16*>(scale), scale_bstride, scale_sstride,
                            static_cast<const __nv_bfloat16*>(shift), shift_bstride, shift_sstride, o);
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "adanorm launch");
   return LTXFP8_OK;
 }
@@ -445,11 +453,10 @@ int ltxfp8_rms_fma(void* x, const void* y, int64_t B, int64_t S, int64_t H, cons
   DeviceInfo* d;
   rc = device_info(&d);
   if (rc) return rc;
-  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
-  LTXFP8_PRODUCER_DISPATCH(rms_fma_launch, producer_chunks(H), flags, grid, static_cast<cudaStream_t>(stream),
+  cudaError_t e = cudaSuccess;
+  LTXFP8_PRODUCER_DISPATCH(e, rms_fma_launch, producer_chunks(H), flags, d, static_cast<cudaStream_t>(stream),
                            static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), M, S,
                            static_cast<int>(H), static_cast<const __nv_bfloat16*>(z), z_bstride, z_sstride, o);
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rms_fma launch");
   return LTXFP8_OK;
 }
@@ -458,8 +465,9 @@ int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtyp
                            int64_t heads, void* q, float* sfa, int64_t sfa_ld, void* out, int flags, void* stream) {
   int rc = producer_check("gated_attention", M, H, flags);
   if (rc) return rc;
-  if (heads <= 0 || H % heads != 0 || (H / heads) % 8 != 0)
-    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gated_attention: H / heads must be a multiple of 8 (H=%lld heads=%lld)",
+  if (heads <= 0 || heads > 64 || H % heads != 0 || (H / heads) % 8 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE,
+                "gated_attention: need 1 <= heads <= 64 and H / heads a multiple of 8 (H=%lld heads=%lld)",
                 (long long)H, (long long)heads);
   if (gate_dtype != LTXFP8_DTYPE_BF16 && gate_dtype != LTXFP8_DTYPE_F32)
     return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gated_attention: gate logits must be bf16 or fp32");
@@ -473,11 +481,10 @@ int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtyp
   DeviceInfo* d;
   rc = device_info(&d);
   if (rc) return rc;
-  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
-  LTXFP8_PRODUCER_DISPATCH(gated_launch, producer_chunks(H), flags, grid, static_cast<cudaStream_t>(stream),
+  cudaError_t e = cudaSuccess;
+  LTXFP8_PRODUCER_DISPATCH(e, gated_launch, producer_chunks(H), flags, d, static_cast<cudaStream_t>(stream),
                            static_cast<const __nv_bfloat16*>(x), gate_logits, gate_dtype == LTXFP8_DTYPE_F32, M,
                            static_cast<int>(H), static_cast<int>(heads), o);
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gated_attention launch");
   return LTXFP8_OK;
 }

@@ -104,21 +104,17 @@ __device__ __forceinline__ void quant_group8(const float (&f)[8], bool valid, ui
   }
 }
 
-// Sum over this lane's chunks of bf16(v*v), chunk by chunk, element by element.
-template <int kChunks>
-__device__ __forceinline__ float lane_sumsq_bf16(const uint4 (&v)[kChunks], int lane, int nchunks) {
-  float acc = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kChunks; ++i) {
-    if (i * 32 + lane < nchunks) {
-      float f[8];
-      bf16x8_to_f32(v[i], f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, bf16_rn(__fmul_rn(f[j], f[j])));
-    }
-  }
-  return acc;
-}
+// bf16x2 lanes of a 16-byte chunk.  bf16 sums and products computed in fp32 and
+// rounded once equal the correctly rounded bf16 operations: a product of two
+// bf16 values is exact in fp32, and a sum whose fp32 rounding is inexact has its
+// addends more than 16 binades apart, which keeps it off every bf16 midpoint.
+// So the packed __hadd2 / __hmul2_rn below compute bf16(a + b) and bf16(a * b)
+// (the _rn multiply keeps the compiler from contracting a product and a following
+// sum into one fused rounding).
+__device__ __forceinline__ __nv_bfloat162 bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ uint32_t u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ float2 f2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+__device__ __forceinline__ uint32_t word(const uint4& v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
 
 struct ProducerOut {
   uint8_t* q;      // e4m3 [M, H] or null
@@ -127,9 +123,27 @@ struct ProducerOut {
   __nv_bfloat16* out;  // bf16 [M, H] (unquantised output) or null
 };
 
+// sum += bf16(v*v) over the 8 values of a chunk, in element order.
+__device__ __forceinline__ float sumsq_chunk(float acc, const uint4& v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 x = bf2(word(v, k));
+    const float2 sq = f2(__hmul2_rn(x, x));
+    acc = __fadd_rn(acc, sq.x);
+    acc = __fadd_rn(acc, sq.y);
+  }
+  return acc;
+}
+
+// The norm producers make two passes over a row: the first reduces the row's sum
+// of squares, the second re-reads the row (an L2 hit: the warp read or wrote it
+// microseconds earlier) to normalise and quantise.  Nothing of the row stays in
+// registers between the passes, which keeps the register count low and lets many
+// rows per SM be in flight.
+
 // x bf16 [B*S, H]; scale/shift element (b, s, h) at p[b * bstride + s * sstride + h].
 template <int kChunks, int kMode>
-__global__ void __launch_bounds__(kProdWarps * 32) adanorm_quant_kernel(
+__global__ void __launch_bounds__(kProdWarps * 32, 4) adanorm_quant_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t M, int64_t S, int H, const __nv_bfloat16* __restrict__ scale,
     int64_t scale_bs, int64_t scale_ss, const __nv_bfloat16* __restrict__ shift, int64_t shift_bs, int64_t shift_ss,
     ProducerOut o) {
@@ -138,32 +152,40 @@ __global__ void __launch_bounds__(kProdWarps * 32) adanorm_quant_kernel(
   if (row >= M) return;
   const int nchunks = H / 8;
   const __nv_bfloat16* xr = x + row * H;
-  uint4 v[kChunks];
+  float acc = 0.0f;
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 32 + lane;
-    v[i] = c < nchunks ? ldg16(xr + c * 8) : make_uint4(0, 0, 0, 0);
+    if (c < nchunks) acc = sumsq_chunk(acc, ldg16(xr + c * 8));
   }
   // mean of bf16 squares, + eps, 1/sqrt (triton_ops.py:82-85)
-  const float ss = warp_sum_butterfly(lane_sumsq_bf16<kChunks>(v, lane, nchunks));
+  const float ss = warp_sum_butterfly(acc);
   const float r = rsqrt_ieee(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), 1e-5f));
   const int64_t b = row / S, s = row - b * S;
   const __nv_bfloat16* scr = scale + b * scale_bs + s * scale_ss;
   const __nv_bfloat16* shr = shift + b * shift_bs + s * shift_ss;
+  const __nv_bfloat162 one = __float2bfloat162_rn(1.0f);
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 32 + lane;
     const bool valid = c < nchunks;
     if (i * 32 >= nchunks) break;  // warp-uniform: no group of this load exists
-    float f[8], sc[8], sh[8];
-    bf16x8_to_f32(v[i], f);
-    bf16x8_to_f32(valid ? ldg16(scr + c * 8) : make_uint4(0, 0, 0, 0), sc);
-    bf16x8_to_f32(valid ? ldg16(shr + c * 8) : make_uint4(0, 0, 0, 0), sh);
+    uint4 xv = make_uint4(0, 0, 0, 0), sc = xv, sh = xv;
+    if (valid) {
+      xv = ldg16(xr + c * 8);
+      sc = ldg16(scr + c * 8);
+      sh = ldg16(shr + c * 8);
+    }
+    float f[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float y = bf16_rn(__fmul_rn(f[j], r));           // (x * x_norm).to(bf16)
-      const float t = bf16_rn(__fadd_rn(1.0f, sc[j]));       // 1.0 + norm_scales (bf16)
-      f[j] = bf16_rn(__fadd_rn(bf16_rn(__fmul_rn(y, t)), sh[j]));  // x * t + shift, bf16 steps
+    for (int k = 0; k < 4; ++k) {
+      const float2 xf = f2(bf2(word(xv, k)));
+      // (x * x_norm).to(bf16), then x * (1.0 + norm_scales) + norm_shift in bf16 steps
+      const __nv_bfloat162 y = __float22bfloat162_rn(make_float2(__fmul_rn(xf.x, r), __fmul_rn(xf.y, r)));
+      const __nv_bfloat162 t = __hadd2(one, bf2(word(sc, k)));
+      const float2 z = f2(__hadd2(__hmul2_rn(y, t), bf2(word(sh, k))));
+      f[2 * k] = z.x;
+      f[2 * k + 1] = z.y;
     }
     quant_group8<kMode>(f, valid, o.q + row * H + c * 8, o.sfa + static_cast<int64_t>(c / 16) * o.sfa_ld + row, l16);
   }
@@ -171,12 +193,14 @@ __global__ void __launch_bounds__(kProdWarps * 32) adanorm_quant_kernel(
 
 // x, y bf16 [B*S, H]; z (b, s, h) at z[b * bstride + s * sstride + h].
 // x <- bf16(x + bf16(y z)); o = x * rsqrt(mean(bf16(x^2))) in fp32; quantised
-// (o.q) or rounded to bf16 (o.out).
+// (o.q) or rounded to bf16 (o.out).  The second pass reads back the updated x
+// (this thread's own stores, through the coherent path).
 template <int kChunks, int kMode, bool kQuant>
-__global__ void __launch_bounds__(kProdWarps * 32) rms_fma_kernel(__nv_bfloat16* __restrict__ x,
-                                                                const __nv_bfloat16* __restrict__ y, int64_t M,
-                                                                int64_t S, int H, const __nv_bfloat16* __restrict__ z,
-                                                                int64_t z_bs, int64_t z_ss, ProducerOut o) {
+__global__ void __launch_bounds__(kProdWarps * 32, 4) rms_fma_kernel(__nv_bfloat16* __restrict__ x,
+                                                                   const __nv_bfloat16* __restrict__ y, int64_t M,
+                                                                   int64_t S, int H,
+                                                                   const __nv_bfloat16* __restrict__ z, int64_t z_bs,
+                                                                   int64_t z_ss, ProducerOut o) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l16 = lane & 15;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kProdWarps + warp;
   if (row >= M) return;
@@ -185,24 +209,23 @@ __global__ void __launch_bounds__(kProdWarps * 32) rms_fma_kernel(__nv_bfloat16*
   const __nv_bfloat16* yr = y + row * H;
   const int64_t b = row / S, s = row - b * S;
   const __nv_bfloat16* zr = z + b * z_bs + s * z_ss;
-  uint4 v[kChunks];
+  float acc = 0.0f;
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 32 + lane;
     if (c < nchunks) {
-      float fx[8], fy[8], fz[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(xr + c * 8), fx);
-      bf16x8_to_f32(ldg16(yr + c * 8), fy);
-      bf16x8_to_f32(ldg16(zr + c * 8), fz);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) fx[j] = bf16_rn(__fadd_rn(fx[j], bf16_rn(__fmul_rn(fy[j], fz[j]))));
-      v[i] = pack_bf16x8(fx);
-      *reinterpret_cast<uint4*>(xr + c * 8) = v[i];  // residual stream updated in place
-    } else {
-      v[i] = make_uint4(0, 0, 0, 0);
+      const uint4 xv = *reinterpret_cast<const uint4*>(xr + c * 8);
+      const uint4 yv = ldg16(yr + c * 8), zv = ldg16(zr + c * 8);
+      // bf16(x + bf16(y * z))
+      const uint4 ov = make_uint4(u32(__hadd2(bf2(xv.x), __hmul2_rn(bf2(yv.x), bf2(zv.x)))),
+                                  u32(__hadd2(bf2(xv.y), __hmul2_rn(bf2(yv.y), bf2(zv.y)))),
+                                  u32(__hadd2(bf2(xv.z), __hmul2_rn(bf2(yv.z), bf2(zv.z)))),
+                                  u32(__hadd2(bf2(xv.w), __hmul2_rn(bf2(yv.w), bf2(zv.w)))));
+      *reinterpret_cast<uint4*>(xr + c * 8) = ov;  // residual stream updated in place
+      acc = sumsq_chunk(acc, ov);
     }
   }
-  const float ss = warp_sum_butterfly(lane_sumsq_bf16<kChunks>(v, lane, nchunks));
+  const float ss = warp_sum_butterfly(acc);
   const float r = rsqrt_ieee(__fdiv_rn(ss, static_cast<float>(H)));  // no epsilon (triton_ops.py:222-224)
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
@@ -210,9 +233,9 @@ __global__ void __launch_bounds__(kProdWarps * 32) rms_fma_kernel(__nv_bfloat16*
     const bool valid = c < nchunks;
     if (i * 32 >= nchunks) break;
     float f[8];
-    bf16x8_to_f32(v[i], f);
+    bf16x8_to_f32(valid ? *reinterpret_cast<const uint4*>(xr + c * 8) : make_uint4(0, 0, 0, 0), f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = __fmul_rn(f[j], r);
+    for (int k = 0; k < 8; ++k) f[k] = __fmul_rn(f[k], r);
     if constexpr (kQuant) {
       quant_group8<kMode>(f, valid, o.q + row * H + c * 8, o.sfa + static_cast<int64_t>(c / 16) * o.sfa_ld + row,
                           l16);
@@ -234,6 +257,22 @@ __global__ void __launch_bounds__(kProdWarps * 32) gated_attention_kernel(const 
   const int nchunks = H / 8;
   const int dim_head = H / heads;
   const __nv_bfloat16* xr = x + row * H;
+  // 2 sigmoid(logit) of heads `lane` and `lane + 32` (heads <= 64), broadcast below.
+  float gate_lo = 0.0f, gate_hi = 0.0f;
+#pragma unroll
+  for (int part = 0; part < 2; ++part) {
+    const int h = lane + 32 * part;
+    if (h < heads) {
+      float g;
+      if constexpr (kGateF32) {
+        g = __ldg(static_cast<const float*>(gate_logits) + row * heads + h);
+      } else {
+        g = __bfloat162float(static_cast<const __nv_bfloat16*>(gate_logits)[row * heads + h]);
+      }
+      const float gate = __fmul_rn(2.0f, sigmoid_cw(g));
+      if (part == 0) gate_lo = gate; else gate_hi = gate;
+    }
+  }
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 32 + lane;
@@ -243,13 +282,9 @@ __global__ void __launch_bounds__(kProdWarps * 32) gated_attention_kernel(const 
     bf16x8_to_f32(valid ? ldg16(xr + c * 8) : make_uint4(0, 0, 0, 0), f);
     // dim_head % 8 == 0: a chunk lies within one head
     const int head = valid ? (c * 8) / dim_head : 0;
-    float g;
-    if constexpr (kGateF32) {
-      g = __ldg(static_cast<const float*>(gate_logits) + row * heads + head);
-    } else {
-      g = __bfloat162float(static_cast<const __nv_bfloat16*>(gate_logits)[row * heads + head]);
-    }
-    const float gate = __fmul_rn(2.0f, sigmoid_cw(g));
+    const float glo = __shfl_sync(0xffffffffu, gate_lo, head & 31);
+    const float ghi = __shfl_sync(0xffffffffu, gate_hi, head & 31);
+    const float gate = head < 32 ? glo : ghi;
 #pragma unroll
     for (int j = 0; j < 8; ++j) f[j] = __fmul_rn(f[j], gate);
     if constexpr (kQuant) {
