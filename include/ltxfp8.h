@@ -128,6 +128,36 @@ int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtyp
 int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld, float* sfa,
                                int64_t sfa_ld, int flags, void* stream);
 
+/*
+ * RMSNorm + interleaved RoPE for attention q/k: per row of x bf16 [rows, dim]
+ * (dim % 8 == 0, dim <= 8192), v = x * (rsqrt(sum(x^2) * (1/dim)) * w) (no epsilon;
+ * weights bf16 [dim] or NULL for none), then for each pair (2i, 2i+1)
+ * out[2i] = v[2i] cos[2i] - v[2i+1] sin[2i], out[2i+1] = v[2i+1] cos[2i+1] + v[2i] sin[2i+1],
+ * with cos/sin bf16 rows at p + row * freq_row_stride.  out: bf16 [rows, dim], or
+ * e4m3 (torch's conversion, overflow to NaN) when out_fp8.  Sums of squares in
+ * fp32 with fused multiply-adds in a fixed order; 1/sqrt is an IEEE sqrt and division.
+ * Replaces ops_cpp.rms_norm_rope (ltx-kernels/csrc/ops/rms_norm_rope.cpp:62-114,
+ * rms_norm_rope_cuda.cu:56-175), which is built with --use_fast_math.
+ */
+int ltxfp8_rms_norm_rope(const void* x, int64_t rows, int64_t dim, const void* cos_freqs, const void* sin_freqs,
+                         int64_t freq_row_stride, const void* weights, void* out, int out_fp8, void* stream);
+
+/*
+ * RMSNorm + split RoPE: x bf16 [B, S, H] seen as `heads` heads of d = H / heads
+ * values, each split into halves a = [0, d/2) and b = [d/2, d);
+ * v = (x * rsqrt(sum(x^2) / H + 1e-6)) * w (weights bf16 [H] or NULL), then
+ * out_a = cos v_a - sin v_b, out_b = cos v_b + sin v_a, with cos/sin element
+ * (b, head, s, j) at p[b * bstride + head * hstride + s * sstride + j]
+ * (bstride 0 broadcasts one table over the batch).  d in {16, 32, 64, 128, 256},
+ * H % 128 == 0, H <= 8192.  out: bf16, or saturating e4m3 when out_fp8.
+ * Replaces ops_cpp.rms_norm_split_rope (ltx-kernels/csrc/ops/rms_norm_split_rope.cpp:28-111,
+ * rms_norm_split_rope_cuda.cu:42-150).
+ */
+int ltxfp8_rms_norm_split_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t heads, const void* cos_freqs,
+                               int64_t cos_bstride, int64_t cos_hstride, int64_t cos_sstride, const void* sin_freqs,
+                               int64_t sin_bstride, int64_t sin_hstride, int64_t sin_sstride, const void* weights,
+                               void* out, int out_fp8, void* stream);
+
 /* Epilogue options of ltxfp8_gemm (all zero = plain bias + bf16 store). */
 typedef struct ltxfp8_epilogue {
   int gelu_tanh;          /* apply GELU (tanh approximation) to bf16(acc + bias), rounding to bf16 */

@@ -489,6 +489,97 @@ int ltxfp8_gated_attention(const void* x, const void* gate_logits, int gate_dtyp
   return LTXFP8_OK;
 }
 
+int ltxfp8_rms_norm_rope(const void* x, int64_t rows, int64_t dim, const void* cos_freqs, const void* sin_freqs,
+                         int64_t freq_row_stride, const void* weights, void* out, int out_fp8, void* stream) {
+  if (rows < 0 || dim <= 0 || dim % 8 != 0 || dim > 8192)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "rms_norm_rope: need dim %% 8 == 0, 0 < dim <= 8192 (dim=%lld)",
+                (long long)dim);
+  if (rows == 0) return LTXFP8_OK;
+  if (rows > (static_cast<int64_t>(1) << 31) * kProdWarps) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "rms_norm_rope: too many rows");
+  if (!x || !cos_freqs || !sin_freqs || !out) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "rms_norm_rope: null pointer");
+  if (!aligned(x, 16) || !aligned(cos_freqs, 16) || !aligned(sin_freqs, 16) || !aligned(out, 16) ||
+      (weights && !aligned(weights, 16)) || freq_row_stride % 8 != 0)
+    return fail(LTXFP8_ERR_MISALIGNED, "rms_norm_rope: operands must be 16-byte aligned, freq_row_stride %% 8 == 0");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int ch = producer_chunks(dim);
+  dim3 grid(static_cast<unsigned>((rows + kProdWarps - 1) / kProdWarps));
+  auto s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* cb = static_cast<const __nv_bfloat16*>(cos_freqs);
+  const auto* sb = static_cast<const __nv_bfloat16*>(sin_freqs);
+  const auto* wb = static_cast<const __nv_bfloat16*>(weights);
+  const int di = static_cast<int>(dim);
+#define LTXFP8_ROPE_LAUNCH(C, A, O) \
+  rms_norm_rope_kernel<C, A, O><<<grid, kProdWarps * 32, 0, s>>>(xb, rows, di, cb, sb, freq_row_stride, wb, out)
+#define LTXFP8_ROPE_OUT(C, A) \
+  do { if (out_fp8) LTXFP8_ROPE_LAUNCH(C, A, kRopeE4m3Torch); else LTXFP8_ROPE_LAUNCH(C, A, kRopeBf16); } while (0)
+#define LTXFP8_ROPE_AFF(C) do { if (wb) LTXFP8_ROPE_OUT(C, true); else LTXFP8_ROPE_OUT(C, false); } while (0)
+  switch (ch) {
+    case 4: LTXFP8_ROPE_AFF(4); break;
+    case 8: LTXFP8_ROPE_AFF(8); break;
+    case 16: LTXFP8_ROPE_AFF(16); break;
+    default: LTXFP8_ROPE_AFF(32); break;
+  }
+#undef LTXFP8_ROPE_AFF
+#undef LTXFP8_ROPE_OUT
+#undef LTXFP8_ROPE_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rms_norm_rope launch");
+  return LTXFP8_OK;
+}
+
+int ltxfp8_rms_norm_split_rope(const void* x, int64_t B, int64_t S, int64_t H, int64_t heads, const void* cos_freqs,
+                               int64_t cos_bstride, int64_t cos_hstride, int64_t cos_sstride, const void* sin_freqs,
+                               int64_t sin_bstride, int64_t sin_hstride, int64_t sin_sstride, const void* weights,
+                               void* out, int out_fp8, void* stream) {
+  if (B < 0 || S < 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "rms_norm_split_rope: negative B or S");
+  const int64_t M = B * S;
+  int rc = producer_check("rms_norm_split_rope", M, H, LTXFP8_QUANT_TORCH);
+  if (rc) return rc;
+  const int64_t dh = heads > 0 ? H / heads : 0;
+  if (heads <= 0 || H % heads != 0 || !(dh == 16 || dh == 32 || dh == 64 || dh == 128 || dh == 256))
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "rms_norm_split_rope: head size H / heads must be 16, 32, 64, 128 or 256 "
+                "(H=%lld heads=%lld)", (long long)H, (long long)heads);
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !cos_freqs || !sin_freqs || !out) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "rms_norm_split_rope: null pointer");
+  if (!aligned(x, 16) || !aligned(cos_freqs, 16) || !aligned(sin_freqs, 16) || !aligned(out, 16) ||
+      (weights && !aligned(weights, 16)) || cos_bstride % 8 || cos_hstride % 8 || cos_sstride % 8 || sin_bstride % 8 ||
+      sin_hstride % 8 || sin_sstride % 8)
+    return fail(LTXFP8_ERR_MISALIGNED, "rms_norm_split_rope: operands must be 16-byte aligned, strides %% 8 == 0");
+  DeviceInfo* d;
+  rc = device_info(&d);
+  if (rc) return rc;
+  const int ch = producer_chunks(H);
+  dim3 grid(static_cast<unsigned>((M + kProdWarps - 1) / kProdWarps));
+  auto s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* cb = static_cast<const __nv_bfloat16*>(cos_freqs);
+  const auto* sb = static_cast<const __nv_bfloat16*>(sin_freqs);
+  const auto* wb = static_cast<const __nv_bfloat16*>(weights);
+  const int hi = static_cast<int>(H), ni = static_cast<int>(heads);
+#define LTXFP8_SROPE_LAUNCH(C, A, O)                                                                        \
+  rms_norm_split_rope_kernel<C, A, O><<<grid, kProdWarps * 32, 0, s>>>(xb, B, S, hi, ni, cb, cos_bstride,   \
+                                                                       cos_hstride, cos_sstride, sb,        \
+                                                                       sin_bstride, sin_hstride, sin_sstride, wb, out)
+#define LTXFP8_SROPE_OUT(C, A) \
+  do { if (out_fp8) LTXFP8_SROPE_LAUNCH(C, A, kRopeE4m3Sat); else LTXFP8_SROPE_LAUNCH(C, A, kRopeBf16); } while (0)
+#define LTXFP8_SROPE_AFF(C) do { if (wb) LTXFP8_SROPE_OUT(C, true); else LTXFP8_SROPE_OUT(C, false); } while (0)
+  switch (ch) {
+    case 4: LTXFP8_SROPE_AFF(4); break;
+    case 8: LTXFP8_SROPE_AFF(8); break;
+    case 16: LTXFP8_SROPE_AFF(16); break;
+    default: LTXFP8_SROPE_AFF(32); break;
+  }
+#undef LTXFP8_SROPE_AFF
+#undef LTXFP8_SROPE_OUT
+#undef LTXFP8_SROPE_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rms_norm_split_rope launch");
+  return LTXFP8_OK;
+}
+
 int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld, float* sfa,
                                int64_t sfa_ld, int flags, void* stream) {
   if (M < 0 || K <= 0 || K % 128 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gelu_quantize: need K %% 128 == 0, K > 0, M >= 0 (M=%lld K=%lld)", (long long)M, (long long)K);

@@ -325,4 +325,150 @@ __global__ void __launch_bounds__(256) gelu_quant_kernel(const __nv_bfloat16* __
   }
 }
 
+// ---------------------------------------------------------------------------
+// RMSNorm + RoPE for the attention q/k (ltx-kernels/csrc/ops/rms_norm_rope_cuda.cu,
+// rms_norm_split_rope_cuda.cu).  Row sums of x^2 in fp32 with fused multiply-adds in
+// the lanes' chunk order, then the xor butterfly; 1/sqrt as IEEE sqrt + division.
+
+enum RopeOut : int {
+  kRopeBf16 = 0,       // bf16, round to nearest even
+  kRopeE4m3Torch = 1,  // e4m3 with torch's conversion (overflow -> NaN): c10::Float8_e4m3fn(float)
+  kRopeE4m3Sat = 2,    // e4m3, saturating: __nv_fp8_e4m3(float)
+};
+
+template <int kOut>
+__device__ __forceinline__ void rope_store8(void* out, int64_t elem, const float (&v)[8]) {
+  if constexpr (kOut == kRopeBf16) {
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + elem) = pack_bf16x8(v);
+  } else {
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint16_t lo = kOut == kRopeE4m3Torch ? f32x2_to_e4m3x2(v[4 * i], v[4 * i + 1])
+                                                 : f32x2_to_e4m3x2_inrange(v[4 * i], v[4 * i + 1]);
+      const uint16_t hi = kOut == kRopeE4m3Torch ? f32x2_to_e4m3x2(v[4 * i + 2], v[4 * i + 3])
+                                                 : f32x2_to_e4m3x2_inrange(v[4 * i + 2], v[4 * i + 3]);
+      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    *reinterpret_cast<uint2*>(static_cast<uint8_t*>(out) + elem) = make_uint2(w[0], w[1]);
+  }
+}
+
+// fp32 sum of x^2 over this lane's chunks of a bf16 row (fused multiply-adds in element order).
+template <int kChunks>
+__device__ __forceinline__ float lane_sumsq_f32(const __nv_bfloat16* xr, int lane, int nchunks) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    if (c < nchunks) {
+      float f[8];
+      bf16x8_to_f32(ldg16(xr + c * 8), f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc = fmaf(f[k], f[k], acc);
+    }
+  }
+  return acc;
+}
+
+// Interleaved RoPE: x bf16 [rows, dim]; cos/sin bf16 with row r at p + r * f_rs;
+// w bf16 [dim] or null.  v = x * (rsqrt(sum(x^2) * (1/dim)) [* w]) (no epsilon,
+// rms_norm_rope_cuda.cu:125-150); pairs (2i, 2i+1):
+//   out[2i]   = v[2i] cos[2i] - v[2i+1] sin[2i]      (:160-170)
+//   out[2i+1] = v[2i+1] cos[2i+1] + v[2i] sin[2i+1]
+template <int kChunks, bool kAffine, int kOut>
+__global__ void __launch_bounds__(kProdWarps * 32, 4) rms_norm_rope_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t rows, int dim, const __nv_bfloat16* __restrict__ cosf,
+    const __nv_bfloat16* __restrict__ sinf, int64_t f_rs, const __nv_bfloat16* __restrict__ w, void* __restrict__ out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kProdWarps + warp;
+  if (row >= rows) return;
+  const int nchunks = dim / 8;
+  const __nv_bfloat16* xr = x + row * dim;
+  const float ss = warp_sum_butterfly(lane_sumsq_f32<kChunks>(xr, lane, nchunks));
+  const float n = rsqrt_ieee(__fmul_rn(ss, __frcp_rn(static_cast<float>(dim))));
+  const __nv_bfloat16* cr = cosf + row * f_rs;
+  const __nv_bfloat16* sr = sinf + row * f_rs;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 32 + lane;
+    if (c < nchunks) {
+      float v[8], cs[8], sn[8], o[8];
+      bf16x8_to_f32(ldg16(xr + c * 8), v);
+      bf16x8_to_f32(ldg16(cr + c * 8), cs);
+      bf16x8_to_f32(ldg16(sr + c * 8), sn);
+      if constexpr (kAffine) {
+        float wv[8];
+        bf16x8_to_f32(ldg16(w + c * 8), wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], __fmul_rn(n, wv[k]));
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], n);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {
+        o[k] = fmaf(v[k], cs[k], -__fmul_rn(v[k + 1], sn[k]));
+        o[k + 1] = fmaf(v[k + 1], cs[k + 1], __fmul_rn(v[k], sn[k + 1]));
+      }
+      rope_store8<kOut>(out, row * dim + c * 8, o);
+    }
+  }
+}
+
+// Split RoPE: x bf16 [B, S, H] as heads of d = H / heads values, each head as two
+// halves (first, second) of d/2; cos/sin [B or 1, heads, S, d/2] by strides
+// (sb, sn, ss), inner stride 1.  v = (x * rsqrt(sum(x^2) / H + 1e-6)) [* w]
+// (rms_norm_split_rope_cuda.cu:73-105), then
+//   first[j]  = cos[j] first[j] - sin[j] second[j]
+//   second[j] = cos[j] second[j] + sin[j] first[j]     (:107-140)
+// d/16 (the chunk distance between the halves) is a power of two <= 16, so the
+// partner chunk sits in lane ^ (d/16) of the same load.
+template <int kChunks, bool kAffine, int kOut>
+__global__ void __launch_bounds__(kProdWarps * 32, 4) rms_norm_split_rope_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t B, int64_t S, int H, int heads,
+    const __nv_bfloat16* __restrict__ cosf, int64_t c_sb, int64_t c_sn, int64_t c_ss,
+    const __nv_bfloat16* __restrict__ sinf, int64_t s_sb, int64_t s_sn, int64_t s_ss,
+    const __nv_bfloat16* __restrict__ w, void* __restrict__ out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kProdWarps + warp;
+  if (row >= B * S) return;
+  const int nchunks = H / 8;
+  const int d = H / heads, half = d / 2, partner = d / 16;
+  const __nv_bfloat16* xr = x + row * H;
+  const float ss = warp_sum_butterfly(lane_sumsq_f32<kChunks>(xr, lane, nchunks));
+  const float r = rsqrt_ieee(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), 1e-6f));
+  const int64_t bi = row / S, si = row - bi * S;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    if (i * 32 >= nchunks) break;  // warp-uniform
+    const int c = i * 32 + lane;
+    const bool valid = c < nchunks;
+    float v[8];
+    bf16x8_to_f32(valid ? ldg16(xr + c * 8) : make_uint4(0, 0, 0, 0), v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], r);
+    if constexpr (kAffine) {
+      float wv[8];
+      bf16x8_to_f32(valid ? ldg16(w + c * 8) : make_uint4(0, 0, 0, 0), wv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], wv[k]);
+    }
+    float other[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) other[k] = __shfl_xor_sync(0xffffffffu, v[k], partner);
+    if (valid) {
+      const int e = c * 8, hd = e / d, p = e - hd * d;
+      const bool first = p < half;
+      const int j = first ? p : p - half;
+      float cs[8], sn[8], o[8];
+      bf16x8_to_f32(ldg16(cosf + bi * c_sb + hd * c_sn + si * c_ss + j), cs);
+      bf16x8_to_f32(ldg16(sinf + bi * s_sb + hd * s_sn + si * s_ss + j), sn);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = fmaf(first ? -sn[k] : sn[k], other[k], __fmul_rn(cs[k], v[k]));
+      rope_store8<kOut>(out, row * H + e, o);
+    }
+  }
+}
+
 }  // namespace ltxfp8

@@ -18,9 +18,12 @@ The activation quantiser's arithmetic is selectable (``set_quant_mode``):
   ``blockwise::gated_attention`` and ``blockwise::quantize(use_gelu=True)`` -- the
   fused producers of triton_ops.py:52-345 (csrc/producers.cuh).
 
-Names that belong to other parts of the reference (FP6 packing, RMSNorm+RoPE)
-are exported so the import list resolves, and raise ``NotImplementedError`` when
-called.
+* ``rms_norm_rope`` / ``rms_norm_split_rope`` (ops ``q8_kernels_ops::rms_norm_rope``,
+  ``q8_kernels_ops::rms_norm_split_rope``) -- q/k RMSNorm + RoPE of the reference's
+  ops_cpp extension (csrc/ops/rms_norm*_cuda.cu).
+
+The FP6 packing helpers belong to another quantisation mode; they are exported so
+the import list resolves, and raise ``NotImplementedError`` when called.
 """
 from __future__ import annotations
 
@@ -186,6 +189,45 @@ def gated_attention_triton(x: torch.Tensor, gate_logits: torch.Tensor, quantize:
     return (out, sc) if quantize else (out, None)
 
 
+# ----------------------------------------------------------------------------- RMSNorm + RoPE
+# Same op names and schemas as the reference's ops_cpp registrations
+# (ltx-kernels/src/ltx_kernels/blockwise/functional.py:25-74).
+@torch.library.custom_op("q8_kernels_ops::rms_norm_rope", mutates_args=())
+def _rms_norm_rope_cuda(x: torch.Tensor, weights: Optional[torch.Tensor], cos_freqs: torch.Tensor,
+                        sin_freqs: torch.Tensor, out_16bit: bool) -> torch.Tensor:
+    return ops.rms_norm_rope(x, cos_freqs, sin_freqs, weights, out_fp8=not out_16bit)
+
+
+@_rms_norm_rope_cuda.register_fake
+def _rms_norm_rope_cuda_fake(x, weights, cos_freqs, sin_freqs, out_16bit):
+    return torch.empty(x.shape, dtype=torch.bfloat16 if out_16bit else torch.float8_e4m3fn, device=x.device)
+
+
+@torch.library.custom_op("q8_kernels_ops::rms_norm_split_rope", mutates_args=())
+def _rms_norm_split_rope_cuda(x: torch.Tensor, sin_freqs: torch.Tensor, cos_freqs: torch.Tensor,
+                              weights: torch.Tensor, out_fp8: bool) -> torch.Tensor:
+    return ops.rms_norm_split_rope(x, cos_freqs, sin_freqs, weights, out_fp8=out_fp8)
+
+
+@_rms_norm_split_rope_cuda.register_fake
+def _rms_norm_split_rope_cuda_fake(x, sin_freqs, cos_freqs, weights, out_fp8):
+    return torch.empty(x.shape, dtype=torch.float8_e4m3fn if out_fp8 else torch.bfloat16, device=x.device)
+
+
+def rms_norm_rope(x: torch.Tensor, cos_freqs: torch.Tensor, sin_freqs: torch.Tensor,
+                  weights: Optional[torch.Tensor] = None, out_fp8: bool = False) -> torch.Tensor:
+    """RMSNorm (no epsilon) + interleaved RoPE (functional.py:93-102 of the reference)."""
+    return torch.ops.q8_kernels_ops.rms_norm_rope(x, weights, cos_freqs, sin_freqs, not out_fp8)
+
+
+def rms_norm_split_rope(x: torch.Tensor, cos_freqs: torch.Tensor, sin_freqs: torch.Tensor,
+                        weights: Optional[torch.Tensor] = None, out_fp8: bool = False) -> torch.Tensor:
+    """RMSNorm (eps 1e-6) + split RoPE (functional.py:105-125 of the reference)."""
+    if weights is None:
+        weights = torch.ones(x.shape[-1], dtype=x.dtype, device=x.device)
+    return torch.ops.q8_kernels_ops.rms_norm_split_rope(x, sin_freqs, cos_freqs, weights, out_fp8)
+
+
 run_quant_blockwise_norm_tma_aligned = blockwise_quantize_adanorm_triton
 run_quant_blockwise_rms_fma = blockwise_quantize_rms_fma_triton
 run_rms_fma = rms_fma_triton
@@ -236,5 +278,3 @@ def _not_provided(name: str):
 fp6_blockwise_quantize_weights_torch = _not_provided("fp6_blockwise_quantize_weights_torch")
 fp6_pack_tensor = _not_provided("fp6_pack_tensor")
 fp6_unpack_tensor = _not_provided("fp6_unpack_tensor")
-rms_norm_rope = _not_provided("rms_norm_rope")
-rms_norm_split_rope = _not_provided("rms_norm_split_rope")

@@ -237,6 +237,64 @@ def gelu_quantize_1x128(x: torch.Tensor, mode: int = L.QUANT_TORCH) -> Tuple[tor
     return q, s
 
 
+def rms_norm_rope(x: torch.Tensor, cos_freqs: torch.Tensor, sin_freqs: torch.Tensor,
+                  weights: Optional[torch.Tensor] = None, out_fp8: bool = False) -> torch.Tensor:
+    """RMSNorm + interleaved RoPE over the last dim of bf16 x; cos/sin reshape to (rows, dim)."""
+    _require_cuda("rms_norm_rope", x, cos_freqs, sin_freqs, weights)
+    for name, t in (("x", x), ("cos_freqs", cos_freqs), ("sin_freqs", sin_freqs)):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"rms_norm_rope: {name} must be bf16, got {t.dtype}")
+    dim = x.shape[-1]
+    x2 = x.reshape(-1, dim).contiguous()
+    rows = x2.shape[0]
+    c2 = cos_freqs.reshape(-1, dim).contiguous()
+    s2 = sin_freqs.reshape(-1, dim).contiguous()
+    if c2.shape[0] != rows or s2.shape[0] != rows:
+        raise RuntimeError(f"rms_norm_rope: cos/sin have {c2.shape[0]}/{s2.shape[0]} rows of {dim}, x has {rows}")
+    w = None
+    if weights is not None:
+        if weights.dtype != torch.bfloat16 or weights.numel() != dim:
+            raise RuntimeError("rms_norm_rope: weights must be bf16 [dim]")
+        w = weights.contiguous()
+    out = torch.empty(x.shape, dtype=torch.float8_e4m3fn if out_fp8 else torch.bfloat16, device=x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_rms_norm_rope(x2.data_ptr(), rows, dim, c2.data_ptr(), s2.data_ptr(), dim,
+                                               None if w is None else w.data_ptr(), out.data_ptr(), int(out_fp8),
+                                               _stream(x)))
+    return out
+
+
+def rms_norm_split_rope(x: torch.Tensor, cos_freqs: torch.Tensor, sin_freqs: torch.Tensor,
+                        weights: Optional[torch.Tensor] = None, out_fp8: bool = False) -> torch.Tensor:
+    """RMSNorm + split RoPE: x bf16 [b, s, h]; cos/sin [b or 1, heads, s, d/2] (any outer
+    strides, unit inner stride -- e.g. the swapaxes view of apply_split_rotary_emb)."""
+    _require_cuda("rms_norm_split_rope", x, cos_freqs, sin_freqs, weights)
+    b, s, h = _rows3(x, "rms_norm_split_rope")
+    if cos_freqs.shape != sin_freqs.shape or cos_freqs.dim() != 4:
+        raise RuntimeError("rms_norm_split_rope: cos_freqs and sin_freqs must both be [b, heads, s, d/2]")
+    fb, heads, fs, half = cos_freqs.shape
+    if fb not in (1, b) or fs != s or heads * half * 2 != h:
+        raise RuntimeError(f"rms_norm_split_rope: freq shape {tuple(cos_freqs.shape)} does not match x {tuple(x.shape)}")
+    strides = []
+    for t in (cos_freqs, sin_freqs):
+        if t.dtype != torch.bfloat16 or t.stride(3) != 1:
+            raise RuntimeError("rms_norm_split_rope: freqs must be bf16 with a unit inner stride")
+        strides.append((0 if fb == 1 else t.stride(0), t.stride(1), t.stride(2)))
+    w = None
+    if weights is not None:
+        if weights.dtype != torch.bfloat16 or weights.numel() != h:
+            raise RuntimeError("rms_norm_split_rope: weights must be bf16 [h]")
+        w = weights.contiguous()
+    out = torch.empty(x.shape, dtype=torch.float8_e4m3fn if out_fp8 else torch.bfloat16, device=x.device)
+    (cb, cn, cs), (sb, sn, ss) = strides
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_rms_norm_split_rope(x.data_ptr(), b, s, h, heads, cos_freqs.data_ptr(), cb, cn, cs,
+                                                     sin_freqs.data_ptr(), sb, sn, ss,
+                                                     None if w is None else w.data_ptr(), out.data_ptr(),
+                                                     int(out_fp8), _stream(x)))
+    return out
+
+
 # ----------------------------------------------------------------------------- GEMM
 def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Tensor,
          bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,

@@ -455,3 +455,121 @@ void orc_gelu_quant(const uint16_t* x, int64_t M, int64_t K, uint8_t* q, float* 
     }
     free(row);
 }
+
+/* ------------------------------------------------------------------------
+ * RMSNorm + RoPE for attention q/k (ltx-kernels/csrc/ops/rms_norm_rope_cuda.cu,
+ * rms_norm_split_rope_cuda.cu).  Parity unpinned: the reference builds these with
+ * torch headers and a fast-math flag and they cannot run here.  Restated with the
+ * arithmetic the CUDA kernels fix: sum of x^2 by fused multiply-adds in the lanes'
+ * chunk order then the xor butterfly, 1/sqrt as IEEE sqrt then division.
+ * -------------------------------------------------------------------- */
+
+static float row_sumsq_fma(const float* x, int64_t H) {
+    float part[32];
+    int64_t nchunks = H / 8;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int64_t c = l; c < nchunks; c += 32)
+            for (int j = 0; j < 8; ++j) acc = fmaf(x[c * 8 + j], x[c * 8 + j], acc);
+        part[l] = acc;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        float nxt[32];
+        for (int l = 0; l < 32; ++l) {
+            volatile float s = part[l] + part[l ^ off];
+            nxt[l] = s;
+        }
+        memcpy(part, nxt, sizeof(part));
+    }
+    return part[0];
+}
+
+/* e4m3 with the saturating conversion of __nv_fp8_e4m3(float): finite overflow and
+   infinities become +-448, NaN stays NaN. */
+static uint8_t f32_to_e4m3_sat(float f) {
+    if (f != f) return orc_f32_to_e4m3(f);
+    if (fabsf(f) > 448.0f) return (uint8_t)((bits_from_f32(f) >> 24 & 0x80u) | 0x7Eu);
+    return orc_f32_to_e4m3(f);
+}
+
+static void store_rope(void* out, int64_t idx, float v, int mode) {
+    if (mode == 0) ((uint16_t*)out)[idx] = orc_f32_to_bf16(v);
+    else if (mode == 1) ((uint8_t*)out)[idx] = orc_f32_to_e4m3(v);
+    else ((uint8_t*)out)[idx] = f32_to_e4m3_sat(v);
+}
+
+/*
+ * Interleaved RoPE (rms_norm_rope_cuda.cu:125-170):
+ *   n = rsqrt(sum(x^2) * (1/dim)); v = x * (n * w) (or x * n);
+ *   out[2i] = v[2i] cos[2i] - v[2i+1] sin[2i]; out[2i+1] = v[2i+1] cos[2i+1] + v[2i] sin[2i+1]
+ *   (as fmaf(v0, c, -(v1 s)) and fmaf(v1, c, v0 s)).
+ * cos/sin row r at p + r * f_rs; w may be NULL; out_mode 0 bf16, 1 e4m3 (torch conversion).
+ */
+void orc_rms_norm_rope(const uint16_t* x, int64_t rows, int64_t dim, const uint16_t* cosf, const uint16_t* sinf,
+                       int64_t f_rs, const uint16_t* w, void* out, int out_mode) {
+    float* v = (float*)malloc(sizeof(float) * (size_t)dim);
+    volatile float inv_dim = 1.0f / (float)dim;
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t h = 0; h < dim; ++h) v[h] = orc_bf16_to_f32(x[r * dim + h]);
+        float ss = row_sumsq_fma(v, dim);
+        volatile float m = ss * inv_dim;
+        float n = rsqrt_ieee(m);
+        for (int64_t h = 0; h < dim; ++h) {
+            volatile float sc = w ? n * orc_bf16_to_f32(w[h]) : n;
+            volatile float t = v[h] * sc;
+            v[h] = t;
+        }
+        const uint16_t* cr = cosf + r * f_rs;
+        const uint16_t* sr = sinf + r * f_rs;
+        for (int64_t h = 0; h < dim; h += 2) {
+            volatile float a = v[h + 1] * orc_bf16_to_f32(sr[h]);
+            float o0 = fmaf(v[h], orc_bf16_to_f32(cr[h]), -a);
+            volatile float b = v[h] * orc_bf16_to_f32(sr[h + 1]);
+            float o1 = fmaf(v[h + 1], orc_bf16_to_f32(cr[h + 1]), b);
+            store_rope(out, r * dim + h, o0, out_mode);
+            store_rope(out, r * dim + h + 1, o1, out_mode);
+        }
+    }
+    free(v);
+}
+
+/*
+ * Split RoPE (rms_norm_split_rope_cuda.cu:73-140): heads of d = H / heads, halves
+ * a = [0, d/2), b = [d/2, d); r = rsqrt(sum(x^2) / H + 1e-6); v = (x * r) * w;
+ *   out_a[j] = fmaf(-sin[j], v_b[j], cos[j] v_a[j]); out_b[j] = fmaf(sin[j], v_a[j], cos[j] v_b[j])
+ * cos/sin element (b, head, s, j) at p[b * sb + head * sn + s * ss + j]; w may be NULL;
+ * out_mode 0 bf16, 2 saturating e4m3.
+ */
+void orc_rms_norm_split_rope(const uint16_t* x, int64_t B, int64_t S, int64_t H, int64_t heads,
+                             const uint16_t* cosf, int64_t c_sb, int64_t c_sn, int64_t c_ss,
+                             const uint16_t* sinf, int64_t s_sb, int64_t s_sn, int64_t s_ss,
+                             const uint16_t* w, void* out, int out_mode) {
+    float* v = (float*)malloc(sizeof(float) * (size_t)H);
+    int64_t d = H / heads, half = d / 2;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t s = 0; s < S; ++s) {
+            int64_t r = b * S + s;
+            for (int64_t h = 0; h < H; ++h) v[h] = orc_bf16_to_f32(x[r * H + h]);
+            float ss = row_sumsq_fma(v, H);
+            volatile float mean = ss / (float)H;
+            volatile float me = mean + 1e-6f;
+            float rr = rsqrt_ieee(me);
+            for (int64_t h = 0; h < H; ++h) {
+                volatile float t = v[h] * rr;
+                if (w) { volatile float u = t * orc_bf16_to_f32(w[h]); v[h] = u; }
+                else v[h] = t;
+            }
+            for (int64_t e = 0; e < H; ++e) {
+                int64_t hd = e / d, p = e % d;
+                int first = p < half;
+                int64_t j = first ? p : p - half;
+                float cs = orc_bf16_to_f32(cosf[b * c_sb + hd * c_sn + s * c_ss + j]);
+                float sn = orc_bf16_to_f32(sinf[b * s_sb + hd * s_sn + s * s_ss + j]);
+                float other = v[first ? e + half : e - half];
+                volatile float cv = cs * v[e];
+                float o = fmaf(first ? -sn : sn, other, cv);
+                store_rope(out, r * H + e, o, out_mode);
+            }
+        }
+    free(v);
+}

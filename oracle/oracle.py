@@ -63,6 +63,9 @@ def lib():
         L.orc_rms_fma.argtypes = [vp, vp, i64, i64, i64, vp, i64, i64, vp, vp, i64, vp]
         L.orc_gated_attention.argtypes = [vp, vp, i32, i64, i64, i64, vp, vp, i64, vp]
         L.orc_gelu_quant.argtypes = [vp, i64, i64, vp, vp, i64]
+        L.orc_rms_norm_rope.argtypes = [vp, i64, i64, vp, vp, i64, vp, vp, i32]
+        L.orc_rms_norm_split_rope.argtypes = [vp, i64, i64, i64, i64, vp, i64, i64, i64, vp, i64, i64, i64, vp, vp,
+                                              i32]
         L.orc_exp_cw.argtypes = [f32]
         L.orc_exp_cw.restype = f32
         _lib = L
@@ -234,6 +237,32 @@ def gelu_quant(x: np.ndarray, sfa_ld: int | None = None):
     sfa = np.full((K // 128, ld), np.nan, np.float32)
     lib().orc_gelu_quant(_p(x), M, K, _p(q), _p(sfa), ld)
     return q, sfa
+
+
+def rms_norm_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, w: np.ndarray | None = None,
+                  out_fp8: bool = False) -> np.ndarray:
+    """Interleaved RoPE after RMSNorm; x, cos, sin [rows, dim] bf16 bits, w [dim] or None.
+    Returns bf16 bits, or e4m3 codes (torch conversion) when out_fp8."""
+    x, cos, sin = _u16(x), _u16(cos), _u16(sin)
+    rows, dim = x.shape
+    out = np.empty((rows, dim), np.uint8 if out_fp8 else np.uint16)
+    lib().orc_rms_norm_rope(_p(x), rows, dim, _p(cos), _p(sin), dim, None if w is None else _p(_u16(w)), _p(out),
+                            1 if out_fp8 else 0)
+    return out
+
+
+def rms_norm_split_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, w: np.ndarray | None = None,
+                        out_fp8: bool = False) -> np.ndarray:
+    """Split RoPE after RMSNorm; x [B, S, H], cos/sin [B or 1, heads, S, d/2] bf16 bits
+    (contiguous; batch 1 broadcasts).  Returns bf16 bits or saturating e4m3 codes."""
+    x, cos, sin = _u16(x), _u16(cos), _u16(sin)
+    B, S, H = x.shape
+    fb, heads, fs, half = cos.shape
+    sb = 0 if fb == 1 else heads * fs * half
+    out = np.empty((B, S, H), np.uint8 if out_fp8 else np.uint16)
+    lib().orc_rms_norm_split_rope(_p(x), B, S, H, heads, _p(cos), sb, fs * half, half, _p(sin), sb, fs * half, half,
+                                  None if w is None else _p(_u16(w)), _p(out), 2 if out_fp8 else 0)
+    return out
 
 
 def exp_cw(x: float) -> float:

@@ -169,3 +169,53 @@ def test_producers_triton_mode_close(cuda_device):
     ua = sa.t().contiguous().view(torch.int32).long()
     ub = sb.t().contiguous().view(torch.int32).long()
     assert (ua - ub).abs().max().item() <= 4
+
+
+def _rope_tables(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    ang = (torch.rand(shape, generator=g) * 2 - 1) * 3.14159
+    return ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("rows,dim,affine,out_fp8", [(64, 4096, True, False), (37, 2048, False, False),
+                                                     (20, 1000, True, False), (16, 4096, True, True)])
+def test_rms_norm_rope_bit_exact(cuda_device, rows, dim, affine, out_fp8):
+    import ltx_kernels.blockwise.functional as F
+    x = activations(rows, dim, seed=dim + rows)
+    cos, sin = _rope_tables((rows, dim), seed=rows)
+    w = (torch.randn(dim, generator=torch.Generator().manual_seed(5)) * 0.2 + 1).to(torch.bfloat16) if affine else None
+    out = F.rms_norm_rope(x.view(1, rows, dim).to(cuda_device), cos.view(1, rows, dim).to(cuda_device),
+                          sin.view(1, rows, dim).to(cuda_device), None if w is None else w.to(cuda_device), out_fp8)
+    torch.cuda.synchronize()
+    ref = O.rms_norm_rope(bits(x), bits(cos), bits(sin), None if w is None else bits(w), out_fp8)
+    if out_fp8:
+        assert O.codes_equal(bits(out).reshape(rows, dim), ref).all()
+    else:
+        assert np.array_equal(bits(out).reshape(rows, dim), ref)
+
+
+@pytest.mark.parametrize("B,S,H,heads,bcast,swapped,out_fp8", [
+    (2, 33, 4096, 32, True, True, False),    # the DiT video q/k: d = 128, freq table shared over the batch
+    (1, 20, 2048, 32, False, False, False),  # d = 64
+    (2, 9, 4096, 16, False, True, False),    # d = 256
+    (1, 17, 1152, 36, True, False, False),   # d = 32, H % 256 == 128
+    (2, 8, 4096, 32, False, True, True),     # saturating e4m3 output
+])
+def test_rms_norm_split_rope_bit_exact(cuda_device, B, S, H, heads, bcast, swapped, out_fp8):
+    import ltx_kernels.blockwise.functional as F
+    d = H // heads
+    x = activations(B * S, H, seed=H + S).view(B, S, H)
+    fb = 1 if bcast else B
+    cos, sin = _rope_tables((fb, heads, S, d // 2), seed=S)
+    w = (torch.randn(H, generator=torch.Generator().manual_seed(6)) * 0.2 + 1).to(torch.bfloat16)
+    cd, sd = cos.to(cuda_device), sin.to(cuda_device)
+    if swapped:  # logical [b, n, s, d/2] over a physical [b, s, n, d/2] buffer, as apply_split_rotary_emb hands it
+        cd = cd.transpose(1, 2).contiguous().transpose(1, 2)
+        sd = sd.transpose(1, 2).contiguous().transpose(1, 2)
+    out = F.rms_norm_split_rope(x.to(cuda_device), cd, sd, w.to(cuda_device), out_fp8)
+    torch.cuda.synchronize()
+    ref = O.rms_norm_split_rope(bits(x), bits(cos), bits(sin), bits(w), out_fp8)
+    if out_fp8:
+        assert O.codes_equal(bits(out), ref).all()
+    else:
+        assert np.array_equal(bits(out), ref)

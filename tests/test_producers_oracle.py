@@ -111,3 +111,47 @@ def test_gated_attention_rejects_bad_heads_without_device():
     assert rc == _lib.ERR_UNSUPPORTED_SHAPE
     rc = L.ltxfp8_gated_attention(16, 16, _lib.DTYPE_BF16, 4, 2048, 512, 16, 16, 4, None, 0, None)
     assert rc == _lib.ERR_UNSUPPORTED_SHAPE  # dim_head 4 is not a multiple of 8
+
+
+def _rope_tables(rows, dim, seed):
+    g = np.random.default_rng(seed)
+    ang = g.uniform(-np.pi, np.pi, (rows, dim))
+    return O.f32_to_bf16(np.cos(ang).astype(np.float32)), O.f32_to_bf16(np.sin(ang).astype(np.float32))
+
+
+def test_rms_norm_rope_restatement_follows_formula():
+    """x / rms(x) * w, then the interleaved rotation of ltx-core's rope.py (pairs (2i, 2i+1))."""
+    rows, dim = 12, 4096
+    x = bits(activations(rows, dim, seed=10))
+    cos, sin = _rope_tables(rows, dim, 11)
+    w = _param(1, 1, dim, 12, std=0.3)[0, 0] + 0  # weights around 1
+    w = O.f32_to_bf16((1.0 + O.bf16_to_f32(w)).astype(np.float32))
+    out = O.rms_norm_rope(x, cos, sin, w)
+    xf = _f64(x)
+    v = xf / np.sqrt((xf * xf).mean(-1, keepdims=True)) * _f64(w)
+    c, s = _f64(cos), _f64(sin)
+    rot = np.empty_like(v)
+    rot[:, 0::2], rot[:, 1::2] = -v[:, 1::2], v[:, 0::2]
+    assert _rel(_f64(out), v * c + rot * s) < BF16_REL
+    q = O.rms_norm_rope(x, cos, sin, w, out_fp8=True)
+    assert _rel(O.e4m3_to_f32(q).astype(np.float64), v * c + rot * s) < 0.06  # plain e4m3 cast, no scales
+
+
+def test_rms_norm_split_rope_restatement_follows_formula():
+    """(x / rms(x)) * w per head split into halves a, b: (a cos - b sin, b cos + a sin)."""
+    B, S, H, heads = 2, 5, 2048, 16
+    d = H // heads
+    x = bits(activations(B * S, H, seed=13)).reshape(B, S, H)
+    g = np.random.default_rng(14)
+    ang = g.uniform(-np.pi, np.pi, (1, heads, S, d // 2))
+    cos = O.f32_to_bf16(np.cos(ang).astype(np.float32))
+    sin = O.f32_to_bf16(np.sin(ang).astype(np.float32))
+    out = O.rms_norm_split_rope(x, cos, sin)
+    xf = _f64(x)
+    v = xf / np.sqrt((xf * xf).mean(-1, keepdims=True) + 1e-6)
+    vh = v.reshape(B, S, heads, 2, d // 2)
+    c = np.transpose(_f64(cos), (0, 2, 1, 3))[:, :, :, None, :]   # [1, S, heads, 1, d/2]
+    s = np.transpose(_f64(sin), (0, 2, 1, 3))[:, :, :, None, :]
+    a, b = vh[:, :, :, 0:1, :], vh[:, :, :, 1:2, :]
+    ref = np.concatenate([a * c - b * s, b * c + a * s], axis=3).reshape(B, S, H)
+    assert _rel(_f64(out), ref) < BF16_REL
