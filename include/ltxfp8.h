@@ -81,6 +81,18 @@ int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stri
                             int64_t K, void* out, void* stream);
 
 /*
+ * Load-time LoRA merge into a blockwise-FP8 weight:
+ *   (q_out, sfb_out) = 128x128 quant of bf16(bf16(e4m3(q) * sfb) + delta)
+ * q e4m3 [N, K], sfb fp32 [N/128, K/128], delta bf16 [N, K] (the aggregated LoRA
+ * update sum (B * strength) @ A); N, K multiples of 128.  q_out / sfb_out may be q /
+ * sfb (in place).  Replaces _blockwise_fp8_fuse
+ * (ltx-core/src/ltx_core/quantization/blockwise/_impl.py:263-301), which dequantises,
+ * adds and requantises in three torch/Triton passes.
+ */
+int ltxfp8_lora_fuse_weight(const void* q, const float* sfb, const void* delta, int64_t N, int64_t K, void* q_out,
+                            float* sfb_out, void* stream);
+
+/*
  * Fused producers of the GEMM's A operand.  Rows are tokens of a [B, S, H]
  * bf16 tensor with contiguous rows (row stride H), M = B * S, H % 128 == 0,
  * H <= 8192.  Per-batch/per-token parameter tensors are addressed as

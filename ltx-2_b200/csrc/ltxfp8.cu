@@ -410,6 +410,27 @@ int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stri
   return LTXFP8_OK;
 }
 
+int ltxfp8_lora_fuse_weight(const void* q, const float* sfb, const void* delta, int64_t N, int64_t K, void* q_out,
+                            float* sfb_out, void* stream) {
+  if (N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "lora_fuse_weight: N and K must be positive multiples of 128 (N=%lld K=%lld)",
+                (long long)N, (long long)K);
+  if (!q || !sfb || !delta || !q_out || !sfb_out) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "lora_fuse_weight: null pointer");
+  if (!aligned(q, 16) || !aligned(delta, 16) || !aligned(q_out, 16) || !aligned(sfb, 4) || !aligned(sfb_out, 4))
+    return fail(LTXFP8_ERR_MISALIGNED, "lora_fuse_weight: q, delta, q_out must be 16-byte aligned");
+  if (N / 128 > 65535) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "lora_fuse_weight: N too large");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
+  lora_fuse_weight_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(q), sfb, static_cast<const __nv_bfloat16*>(delta), K, K / 128,
+      static_cast<uint8_t*>(q_out), sfb_out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "lora_fuse_weight launch");
+  return LTXFP8_OK;
+}
+
 int ltxfp8_adanorm_quantize(const void* x, int64_t B, int64_t S, int64_t H, const void* scale,
                             int64_t scale_bstride, int64_t scale_sstride, const void* shift, int64_t shift_bstride,
                             int64_t shift_sstride, void* q, float* sfa, int64_t sfa_ld, int flags, void* stream) {

@@ -89,6 +89,37 @@ __global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat1
   }
 }
 
+// Second half of the 128x128 block quantiser: each of the 256 threads holds 64
+// consecutive values f of one row of the block.  Block abs-max (NaN-propagating,
+// as torch's abs().max()), s = (1/amax)*448, codes e4m3(f*s) with torch's
+// conversion to `qrow` (this thread's 64 bytes), scale 1/s to *scale by thread 0.
+__device__ __forceinline__ void quant_block_128x128_store(const float (&f)[64], float* red, uint8_t* qrow,
+                                                          float* scale) {
+  const int t = threadIdx.x;
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) amax = fmax_nan(amax, fabsf(f[i]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmax_nan(amax, red[i]);
+  const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
+  uint32_t words[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(f[4 * i], s), __fmul_rn(f[4 * i + 1], s));
+    const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(f[4 * i + 2], s), __fmul_rn(f[4 * i + 3], s));
+    words[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(qrow);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+  if (t == 0) *scale = __frcp_rn(s);
+}
+
 // Weight quant over 128x128 blocks: one block of 256 threads per (kb, nb); each
 // thread owns 64 consecutive values of one row.  s = (1/amax)*448, scale = 1/s
 // (ltx-kernels/src/ltx_kernels/blockwise/functional.py:128-135).
@@ -133,28 +164,7 @@ __global__ void __launch_bounds__(256) quant_weight_128x128_kernel(const void* _
       }
     }
   }
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 64; ++i) amax = fmax_nan(amax, fabsf(f[i]));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  if ((t & 31) == 0) red[t >> 5] = amax;
-  __syncthreads();
-  amax = red[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) amax = fmax_nan(amax, red[i]);
-  const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
-  uint32_t words[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint16_t lo = f32x2_to_e4m3x2(__fmul_rn(f[4 * i], s), __fmul_rn(f[4 * i + 1], s));
-    const uint16_t hi = f32x2_to_e4m3x2(__fmul_rn(f[4 * i + 2], s), __fmul_rn(f[4 * i + 3], s));
-    words[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-  }
-  uint4* dst = reinterpret_cast<uint4*>(q + r * K + c0);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
-  if (t == 0) sfb[nb * KB + kb] = __frcp_rn(s);
+  quant_block_128x128_store(f, red, q + r * K + c0, sfb + nb * KB + kb);
 }
 
 // Dequant: out[m, k] = bf16(float(q[m, k]) * scales[m * rs + (k / 128) * cs]).
@@ -186,6 +196,49 @@ __global__ void __launch_bounds__(256) dequant_1x128_kernel(const uint8_t* __res
     dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
     dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
+}
+
+// Load-time LoRA merge into a blockwise-FP8 weight, one 256-thread block per
+// 128x128 block (thread: 64 consecutive values of one row):
+//   w  = bf16(float(code) * scale)        the 2-D dequantisation (_impl.py:263-274)
+//   w' = bf16(w + delta)                   merged = bf16_weight + deltas (_impl.py:296)
+//   (q', scale') = 128x128 quant of w'     fp8_blockwise_quantize_weights_torch (_impl.py:297)
+// q/sfb may alias q_out/sfb_out (each block reads its inputs before writing).
+__global__ void __launch_bounds__(256) lora_fuse_weight_kernel(const uint8_t* q, const float* sfb,
+                                                               const __nv_bfloat16* __restrict__ delta, int64_t K,
+                                                               int64_t KB, uint8_t* q_out, float* sfb_out) {
+  __shared__ float red[8];
+  const int t = threadIdx.x;
+  const int64_t kb = blockIdx.x, nb = blockIdx.y;
+  const int64_t r = nb * 128 + (t >> 1);
+  const int64_t c0 = kb * 128 + (t & 1) * 64;
+  const float s = sfb[nb * KB + kb];
+  float f[64];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(q + r * K + c0 + 16 * i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(
+          static_cast<__nv_fp8x2_storage_t>(w[j] & 0xFFFFu), __NV_E4M3)));
+      const float2 b = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(
+          static_cast<__nv_fp8x2_storage_t>(w[j] >> 16), __NV_E4M3)));
+      f[16 * i + 4 * j] = a.x;
+      f[16 * i + 4 * j + 1] = a.y;
+      f[16 * i + 4 * j + 2] = b.x;
+      f[16 * i + 4 * j + 3] = b.y;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float dl[8];
+    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(delta + r * K + c0 + 8 * i)), dl);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[8 * i + j] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(f[8 * i + j], s)), dl[j]));
+  }
+  __syncthreads();  // every thread of the block has read its codes and the block scale
+  quant_block_128x128_store(f, red, q_out + r * K + c0, sfb_out + nb * KB + kb);
 }
 
 }  // namespace ltxfp8

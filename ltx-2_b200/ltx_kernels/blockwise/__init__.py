@@ -14,6 +14,7 @@ from ltx_kernels.blockwise.functional import (
 )
 from ltx_kernels.blockwise.linear import BlockwiseFP6Linear, BlockwiseFP8Linear
 from ltx_kernels.blockwise.fused import BlockwiseFP8FeedForward, BlockwiseFP8LoRALinear, fp8_linear
+from ltx_kernels.blockwise.lora_fuse import blockwise_fp8_fuse, blockwise_fp8_fuse_rule, merge_loras
 
 __all__ = [
     "BlockwiseFP6Linear",
@@ -21,6 +22,9 @@ __all__ = [
     "BlockwiseFP8FeedForward",
     "BlockwiseFP8LoRALinear",
     "blockwise_dequantize",
+    "blockwise_fp8_fuse",
+    "blockwise_fp8_fuse_rule",
+    "merge_loras",
     "blockwise_quantize_adanorm_triton",
     "blockwise_quantize_rms_fma_triton",
     "fp6_blockwise_quantize_weights_torch",
