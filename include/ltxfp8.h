@@ -73,6 +73,26 @@ int ltxfp8_quantize_weight_128x128(const void* w, int dtype, int64_t N, int64_t 
                                    void* stream);
 
 /*
+ * As ltxfp8_quantize_weight_128x128 with s = (1/amax) * scale_max, 0 < scale_max <= 448:
+ * scale_max 0.1172 gives the FP6-range weights of fp6_blockwise_quantize_weights_torch
+ * (ltx-kernels/src/ltx_kernels/blockwise/functional.py:22,153-154), whose codes keep the
+ * two top exponent bits zero.
+ */
+int ltxfp8_quantize_weight_128x128_scaled(const void* w, int dtype, int64_t N, int64_t K, float scale_max, void* q,
+                                          float* sfb, void* stream);
+
+/*
+ * FP6 packing of e4m3 codes [m, n] (n % 8 == 0) into [m, n * 3 / 4] bytes: each code
+ * keeps bit 7 and bits 4..0 (the two top exponent bits are dropped), four 6-bit values
+ * fill 3 bytes most-significant first; ltxfp8_fp6_unpack restores them with the
+ * dropped bits zero.  Packed buffers 2-byte, unpacked 8-byte aligned.
+ * Replace ops_cpp.fp6_pack / fp6_unpack (ltx-kernels/csrc/ops/fp6_pack.cu:8-211,
+ * fp6_bitpack.cpp:18-73).
+ */
+int ltxfp8_fp6_pack(const void* x, int64_t m, int64_t n, void* out, void* stream);
+int ltxfp8_fp6_unpack(const void* x, int64_t m, int64_t n, void* out, void* stream);
+
+/*
  * 1x128 dequantisation: out[m, k] = bf16(e4m3(q[m, k]) * scales[m * row_stride + (k/128) * col_stride]).
  * K % 128 == 0.  Replaces blockwise::dequantize
  * (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:387-433).

@@ -384,10 +384,68 @@ int ltxfp8_quantize_weight_128x128(const void* w, int dtype, int64_t N, int64_t 
   if (rc) return rc;
   dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
   quant_weight_128x128_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(w, dtype, K, K / 128,
-                                                                                    static_cast<uint8_t*>(q), sfb);
+                                                                                    static_cast<uint8_t*>(q), sfb,
+                                                                                    448.0f);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "quantize_weight launch");
   return LTXFP8_OK;
+}
+
+int ltxfp8_quantize_weight_128x128_scaled(const void* w, int dtype, int64_t N, int64_t K, float scale_max, void* q,
+                                          float* sfb, void* stream) {
+  if (!(scale_max > 0.0f) || !(scale_max <= 448.0f))
+    return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize_weight_scaled: scale_max must be in (0, 448]");
+  if (N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "quantize_weight_scaled: N and K must be positive multiples of 128 (N=%lld K=%lld)", (long long)N, (long long)K);
+  if (dtype < LTXFP8_DTYPE_F32 || dtype > LTXFP8_DTYPE_F16) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize_weight_scaled: unknown dtype %d", dtype);
+  if (!w || !q || !sfb) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "quantize_weight_scaled: null pointer");
+  if (!aligned(w, 16) || !aligned(q, 16) || !aligned(sfb, 4)) return fail(LTXFP8_ERR_MISALIGNED, "quantize_weight_scaled: w and q must be 16-byte aligned");
+  if (N / 128 > 65535) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "quantize_weight_scaled: N too large");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
+  quant_weight_128x128_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(w, dtype, K, K / 128,
+                                                                                    static_cast<uint8_t*>(q), sfb,
+                                                                                    scale_max);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_weight_scaled launch");
+  return LTXFP8_OK;
+}
+
+static int fp6_launch(bool pack, const void* x, int64_t m, int64_t n, void* out, void* stream) {
+  const char* name = pack ? "fp6_pack" : "fp6_unpack";
+  if (m < 0 || n <= 0 || n % 8 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "%s: need n %% 8 == 0, n > 0 (n=%lld)", name, (long long)n);
+  if (m == 0) return LTXFP8_OK;
+  if (!x || !out) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned(pack ? x : out, 8) || !aligned(pack ? out : x, 2))
+    return fail(LTXFP8_ERR_MISALIGNED, "%s: the unpacked buffer must be 8-byte and the packed one 2-byte aligned", name);
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t groups = m * (n / 8);
+  int64_t blocks = (groups + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(d->sms) * 8;
+  if (blocks > cap) blocks = cap;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (pack)
+    fp6_pack_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(static_cast<const uint8_t*>(x), groups,
+                                                                   static_cast<uint8_t*>(out));
+  else
+    fp6_unpack_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(static_cast<const uint8_t*>(x), groups,
+                                                                     static_cast<uint8_t*>(out));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return LTXFP8_OK;
+}
+
+int ltxfp8_fp6_pack(const void* x, int64_t m, int64_t n, void* out, void* stream) {
+  return fp6_launch(true, x, m, n, out, stream);
+}
+
+int ltxfp8_fp6_unpack(const void* x, int64_t m, int64_t n, void* out, void* stream) {
+  return fp6_launch(false, x, m, n, out, stream);
 }
 
 int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stride, int64_t col_stride, int64_t M,

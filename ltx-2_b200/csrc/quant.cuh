@@ -91,10 +91,10 @@ __global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat1
 
 // Second half of the 128x128 block quantiser: each of the 256 threads holds 64
 // consecutive values f of one row of the block.  Block abs-max (NaN-propagating,
-// as torch's abs().max()), s = (1/amax)*448, codes e4m3(f*s) with torch's
+// as torch's abs().max()), s = (1/amax)*scale_max, codes e4m3(f*s) with torch's
 // conversion to `qrow` (this thread's 64 bytes), scale 1/s to *scale by thread 0.
 __device__ __forceinline__ void quant_block_128x128_store(const float (&f)[64], float* red, uint8_t* qrow,
-                                                          float* scale) {
+                                                          float* scale, float scale_max = 448.0f) {
   const int t = threadIdx.x;
   float amax = 0.0f;
 #pragma unroll
@@ -106,7 +106,7 @@ __device__ __forceinline__ void quant_block_128x128_store(const float (&f)[64], 
   amax = red[0];
 #pragma unroll
   for (int i = 1; i < 8; ++i) amax = fmax_nan(amax, red[i]);
-  const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
+  const float s = __fmul_rn(__frcp_rn(amax), scale_max);
   uint32_t words[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -126,7 +126,7 @@ __device__ __forceinline__ void quant_block_128x128_store(const float (&f)[64], 
 // in_dtype: 0 = fp32, 1 = bf16, 2 = fp16.
 __global__ void __launch_bounds__(256) quant_weight_128x128_kernel(const void* __restrict__ w, int in_dtype, int64_t K,
                                                                    int64_t KB, uint8_t* __restrict__ q,
-                                                                   float* __restrict__ sfb) {
+                                                                   float* __restrict__ sfb, float scale_max) {
   __shared__ float red[8];
   const int t = threadIdx.x;
   const int64_t kb = blockIdx.x, nb = blockIdx.y;
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(256) quant_weight_128x128_kernel(const void* _
       }
     }
   }
-  quant_block_128x128_store(f, red, q + r * K + c0, sfb + nb * KB + kb);
+  quant_block_128x128_store(f, red, q + r * K + c0, sfb + nb * KB + kb, scale_max);
 }
 
 // Dequant: out[m, k] = bf16(float(q[m, k]) * scales[m * rs + (k / 128) * cs]).
@@ -239,6 +239,66 @@ __global__ void __launch_bounds__(256) lora_fuse_weight_kernel(const uint8_t* q,
   }
   __syncthreads();  // every thread of the block has read its codes and the block scale
   quant_block_128x128_store(f, red, q_out + r * K + c0, sfb_out + nb * KB + kb);
+}
+
+// FP6 packing (ltx-kernels/csrc/ops/fp6_pack.cu:8-41,90-112): an e4m3 code whose
+// two top exponent bits are zero keeps its sign (bit 7) and bits 4..0 as a 6-bit
+// value; four values v0..v3 fill 3 bytes most-significant first
+// (v0 << 18 | v1 << 12 | v2 << 6 | v3, high byte first).  Unpacking restores the
+// two dropped bits as zero.  One thread per 8 codes <-> 6 packed bytes.
+__global__ void __launch_bounds__(256) fp6_pack_kernel(const uint8_t* __restrict__ x, int64_t groups,
+                                                       uint8_t* __restrict__ out) {
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(x + g * 8));
+    uint32_t p[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t w = h == 0 ? v.x : v.y;
+      uint32_t acc = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t b = (w >> (8 * i)) & 0xFFu;
+        acc = (acc << 6) | ((b & 0x80u) >> 2) | (b & 0x1Fu);
+      }
+      p[h] = acc;  // 24 bits, v0 in the top six
+    }
+    const uint8_t bytes[6] = {static_cast<uint8_t>(p[0] >> 16), static_cast<uint8_t>(p[0] >> 8),
+                              static_cast<uint8_t>(p[0]), static_cast<uint8_t>(p[1] >> 16),
+                              static_cast<uint8_t>(p[1] >> 8), static_cast<uint8_t>(p[1])};
+    uint16_t* o = reinterpret_cast<uint16_t*>(out + g * 6);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) o[i] = static_cast<uint16_t>(bytes[2 * i] | (bytes[2 * i + 1] << 8));
+  }
+}
+
+__global__ void __launch_bounds__(256) fp6_unpack_kernel(const uint8_t* __restrict__ x, int64_t groups,
+                                                         uint8_t* __restrict__ out) {
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint16_t* in = reinterpret_cast<const uint16_t*>(x + g * 6);
+    uint8_t bytes[6];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const uint16_t u = __ldg(in + i);
+      bytes[2 * i] = static_cast<uint8_t>(u & 0xFFu);
+      bytes[2 * i + 1] = static_cast<uint8_t>(u >> 8);
+    }
+    uint32_t w[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t p = (static_cast<uint32_t>(bytes[3 * h]) << 16) | (static_cast<uint32_t>(bytes[3 * h + 1]) << 8) |
+                         bytes[3 * h + 2];
+      uint32_t word = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t v6 = (p >> (18 - 6 * i)) & 0x3Fu;
+        word |= (((v6 & 0x20u) << 2) | (v6 & 0x1Fu)) << (8 * i);
+      }
+      w[h] = word;
+    }
+    *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);
+  }
 }
 
 }  // namespace ltxfp8

@@ -77,6 +77,9 @@ SIGNATURES = {
     "ltxfp8_rms_norm_split_rope": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
                                           _vp, _vp, _i32, _vp]),
     "ltxfp8_lora_fuse_weight": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "ltxfp8_quantize_weight_128x128_scaled": (_i32, [_vp, _i32, _i64, _i64, _f32, _vp, _vp, _vp]),
+    "ltxfp8_fp6_pack": (_i32, [_vp, _i64, _i64, _vp, _vp]),
+    "ltxfp8_fp6_unpack": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "ltxfp8_gemm_static_scratch": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                            ctypes.POINTER(Epilogue), _vp]),
     "ltxfp8_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _i32, _vp]),

@@ -21,9 +21,8 @@ The activation quantiser's arithmetic is selectable (``set_quant_mode``):
 * ``rms_norm_rope`` / ``rms_norm_split_rope`` (ops ``q8_kernels_ops::rms_norm_rope``,
   ``q8_kernels_ops::rms_norm_split_rope``) -- q/k RMSNorm + RoPE of the reference's
   ops_cpp extension (csrc/ops/rms_norm*_cuda.cu).
-
-The FP6 packing helpers belong to another quantisation mode; they are exported so
-the import list resolves, and raise ``NotImplementedError`` when called.
+* FP6 weights: ``fp6_blockwise_quantize_weights_torch``, ``fp6_pack_tensor`` /
+  ``fp6_unpack_tensor`` (ops ``q8_kernels_ops::fp6_pack`` / ``fp6_unpack``).
 """
 from __future__ import annotations
 
@@ -247,9 +246,9 @@ def blockwise_dequantize(x: Tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
 def blockwise_quantize_weights(w: torch.Tensor, block_size: int = 128,
                                scale_max: float = FP8_SCALE_MAX) -> Tuple[torch.Tensor, torch.Tensor]:
     """W ``[N, K]`` -> (e4m3 ``[N, K]``, fp32 ``[N/128, K/128]``), functional.py:128-135."""
-    if block_size != 128 or scale_max != FP8_SCALE_MAX:
-        raise NotImplementedError("only 128x128 blocks with the e4m3 range (448) are provided")
-    return ops.quantize_weight_128x128(w)
+    if block_size != 128:
+        raise NotImplementedError("only 128x128 blocks are provided")
+    return ops.quantize_weight_128x128(w, scale_max)
 
 
 def fp8_blockwise_quantize_weights_torch(x: torch.Tensor, block_size: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -268,13 +267,41 @@ def blockwise_quantize_torch(x: torch.Tensor, block_size: int = 128,
     return q.view(b, n, h), s.t().contiguous()
 
 
-def _not_provided(name: str):
-    def fn(*args, **kwargs):
-        raise NotImplementedError(f"{name} is outside the blockwise-FP8 linear path ltx-2_b200 provides")
-    fn.__name__ = name
-    return fn
+def fp6_blockwise_quantize_weights_torch(x: torch.Tensor, block_size: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """128x128 weight quant into the FP6 range (scale_max 0.1172, functional.py:153-154)."""
+    return blockwise_quantize_weights(x, block_size, FP6_SCALE_MAX)
 
 
-fp6_blockwise_quantize_weights_torch = _not_provided("fp6_blockwise_quantize_weights_torch")
-fp6_pack_tensor = _not_provided("fp6_pack_tensor")
-fp6_unpack_tensor = _not_provided("fp6_unpack_tensor")
+@torch.library.custom_op("q8_kernels_ops::fp6_pack", mutates_args=())
+def _fp6_pack(x: torch.Tensor) -> torch.Tensor:
+    """e4m3 codes [m, n] -> 6-bit packed uint8 [m, n*3/4] (functional.py:163-178)."""
+    return ops.fp6_pack(x)
+
+
+@_fp6_pack.register_fake
+def _fp6_pack_fake(x: torch.Tensor) -> torch.Tensor:
+    m, n = x.shape
+    return torch.empty(m, (n * 3) // 4, dtype=torch.uint8, device=x.device)
+
+
+@torch.library.custom_op("q8_kernels_ops::fp6_unpack", mutates_args=())
+def _fp6_unpack(x: torch.Tensor, original_n: int) -> torch.Tensor:
+    """6-bit packed uint8 [m, n*3/4] -> e4m3 codes uint8 [m, n] (functional.py:181-197)."""
+    return ops.fp6_unpack(x, original_n)
+
+
+@_fp6_unpack.register_fake
+def _fp6_unpack_fake(x: torch.Tensor, original_n: int) -> torch.Tensor:
+    return torch.empty(x.shape[0], original_n, dtype=torch.uint8, device=x.device)
+
+
+def fp6_pack_tensor(x: torch.Tensor) -> torch.Tensor:
+    return torch.ops.q8_kernels_ops.fp6_pack(x)
+
+
+def fp6_unpack_tensor(x: torch.Tensor, original_n: int) -> torch.Tensor:
+    return torch.ops.q8_kernels_ops.fp6_unpack(x, original_n)
+
+
+fp6_pack = fp6_pack_tensor
+fp6_unpack = fp6_unpack_tensor

@@ -132,12 +132,34 @@ class BlockwiseFP8Linear(BlockwiseLinear):
 
 
 class BlockwiseFP6Linear(BlockwiseLinear):
-    """Packed-FP6 weights (linear.py:212-284) are outside the FP8 path this package
-    rebuilds; the class exists so ltx-core's blockwise module imports resolve."""
+    """FP6-range weights stored 6-bit packed ``[out, in*3/4]`` uint8 with fp32 128x128
+    block scales ``[out/128, in/128]`` (linear.py:212-284).  The forward pass unpacks
+    the codes to e4m3 (the dropped exponent bits are zero) and runs the FP8 GEMM."""
 
-    def __init__(self, *args, **kwargs):
-        raise NotImplementedError("BlockwiseFP6Linear (packed FP6 weights) is not provided by ltx-2_b200")
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None, dtype=None):
+        assert in_features % 8 == 0, f"in_features must be divisible by 8 for fp6_pack, got {in_features}"
+        assert in_features % 128 == 0, f"in_features must be divisible by 128, got {in_features}"
+        assert out_features % 128 == 0, f"out_features must be divisible by 128, got {out_features}"
+        super().__init__(in_features, out_features, bias, device, dtype)
+        self.weight = nn.Parameter(torch.empty(out_features, (in_features // 4) * 3, device=device, dtype=torch.uint8),
+                                   requires_grad=False)
+        self.weight_scale = nn.Parameter(
+            torch.ones(out_features // 128, in_features // 128, device=device, dtype=torch.float32),
+            requires_grad=False)
+
+    @property
+    def fp8weight(self):
+        from .functional import fp6_unpack_tensor
+        return fp6_unpack_tensor(self.weight, self.in_features).view(torch.float8_e4m3fn)
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, transform_weights=True):
-        raise NotImplementedError("BlockwiseFP6Linear (packed FP6 weights) is not provided by ltx-2_b200")
+        from .functional import fp6_blockwise_quantize_weights_torch, fp6_pack_tensor
+        layer = cls(linear.in_features, linear.out_features, linear.bias is not None, device=linear.weight.device)
+        if transform_weights:
+            w_fp6, w_scales = fp6_blockwise_quantize_weights_torch(linear.weight.data.cuda())
+            layer.weight.data = fp6_pack_tensor(w_fp6.view(torch.uint8))
+            layer.weight_scale.data = w_scales
+        if linear.bias is not None:
+            layer.bias.data = linear.bias.data.to(torch.float32)
+        return layer

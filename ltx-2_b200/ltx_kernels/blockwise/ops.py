@@ -94,8 +94,8 @@ def quantize_1x128(x: torch.Tensor, mode: int = L.QUANT_TORCH) -> Tuple[torch.Te
     return q, s
 
 
-def quantize_weight_128x128(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """W [N, K] (fp32/bf16/fp16) -> (e4m3 [N, K], fp32 scales [N/128, K/128])."""
+def quantize_weight_128x128(w: torch.Tensor, scale_max: float = 448.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """W [N, K] (fp32/bf16/fp16) -> (e4m3 [N, K], fp32 scales [N/128, K/128]); s = (1/amax)*scale_max."""
     _require_cuda("quantize_weight_128x128", w)
     dt = {torch.float32: L.DTYPE_F32, torch.bfloat16: L.DTYPE_BF16, torch.float16: L.DTYPE_F16}.get(w.dtype)
     if dt is None:
@@ -107,9 +107,41 @@ def quantize_weight_128x128(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor
     q = torch.empty((N, K), dtype=torch.float8_e4m3fn, device=w.device)
     s = torch.empty((N // 128, K // 128), dtype=torch.float32, device=w.device)
     with _DeviceGuard(w):
-        L.check(L.load().ltxfp8_quantize_weight_128x128(w.data_ptr(), dt, N, K, q.data_ptr(), s.data_ptr(),
-                                                         _stream(w)))
+        if scale_max == 448.0:
+            L.check(L.load().ltxfp8_quantize_weight_128x128(w.data_ptr(), dt, N, K, q.data_ptr(), s.data_ptr(),
+                                                             _stream(w)))
+        else:
+            L.check(L.load().ltxfp8_quantize_weight_128x128_scaled(w.data_ptr(), dt, N, K, float(scale_max),
+                                                                    q.data_ptr(), s.data_ptr(), _stream(w)))
     return q, s
+
+
+def fp6_pack(x: torch.Tensor) -> torch.Tensor:
+    """e4m3 codes (uint8 or float8_e4m3fn) [m, n], n % 8 == 0 -> packed uint8 [m, n*3/4]."""
+    _require_cuda("fp6_pack", x)
+    if x.dim() != 2 or x.element_size() != 1:
+        raise RuntimeError("fp6_pack: expected a 2-D one-byte tensor")
+    x = x.contiguous().view(torch.uint8)
+    m, n = x.shape
+    out = torch.empty((m, n * 3 // 4), dtype=torch.uint8, device=x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_fp6_pack(x.data_ptr(), m, n, out.data_ptr(), _stream(x)))
+    return out
+
+
+def fp6_unpack(x: torch.Tensor, original_n: int) -> torch.Tensor:
+    """Packed uint8 [m, n*3/4] -> e4m3 codes uint8 [m, n] (dropped exponent bits zero)."""
+    _require_cuda("fp6_unpack", x)
+    if x.dim() != 2 or x.dtype != torch.uint8:
+        raise RuntimeError("fp6_unpack: expected a 2-D uint8 tensor")
+    m, npk = x.shape
+    if npk != original_n * 3 // 4:
+        raise RuntimeError(f"fp6_unpack: packed size mismatch: expected {original_n * 3 // 4}, got {npk}")
+    x = x.contiguous()
+    out = torch.empty((m, original_n), dtype=torch.uint8, device=x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_fp6_unpack(x.data_ptr(), m, original_n, out.data_ptr(), _stream(x)))
+    return out
 
 
 def dequantize_1x128(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:

@@ -130,7 +130,7 @@ def quant_act_1x128(x_bf16: np.ndarray, sfa_ld: int | None = None):
     return q, sfa
 
 
-def quant_weight_128x128(w: np.ndarray):
+def quant_weight_128x128(w: np.ndarray, scale_max: float = FP8_SCALE_MAX):
     """Weight quant, 128x128 blocks (functional.py:128-135).  w: float32 or bf16 bits."""
     if w.dtype == np.uint16:
         dt = 1
@@ -142,7 +142,7 @@ def quant_weight_128x128(w: np.ndarray):
     assert N % 128 == 0 and K % 128 == 0
     q = np.empty((N, K), np.uint8)
     s = np.empty((N // 128, K // 128), np.float32)
-    lib().orc_quant_weight_128x128(_p(w), dt, N, K, _p(q), _p(s), FP8_SCALE_MAX)
+    lib().orc_quant_weight_128x128(_p(w), dt, N, K, _p(q), _p(s), scale_max)
     return q, s
 
 
@@ -263,6 +263,25 @@ def rms_norm_split_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, w: np.n
     lib().orc_rms_norm_split_rope(_p(x), B, S, H, heads, _p(cos), sb, fs * half, half, _p(sin), sb, fs * half, half,
                                   None if w is None else _p(_u16(w)), _p(out), 2 if out_fp8 else 0)
     return out
+
+
+def fp6_pack(codes: np.ndarray) -> np.ndarray:
+    """e4m3 codes [m, n] -> [m, n*3/4]: keep bit 7 and bits 4..0 of each code, four 6-bit
+    values per 3 bytes, most significant first (ltx-kernels/csrc/ops/fp6_pack.cu:8-41)."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    m, n = c.shape
+    v = (((c & 0x80) >> 2) | (c & 0x1F)).astype(np.uint32).reshape(m, n // 4, 4)
+    p = (v[..., 0] << 18) | (v[..., 1] << 12) | (v[..., 2] << 6) | v[..., 3]
+    out = np.stack([(p >> 16) & 0xFF, (p >> 8) & 0xFF, p & 0xFF], axis=-1).astype(np.uint8)
+    return out.reshape(m, n * 3 // 4)
+
+
+def fp6_unpack(packed: np.ndarray, n: int) -> np.ndarray:
+    """Inverse of fp6_pack with the two dropped exponent bits zero (fp6_pack.cu:87-103)."""
+    b = np.ascontiguousarray(packed, dtype=np.uint8).reshape(packed.shape[0], n // 4, 3).astype(np.uint32)
+    p = (b[..., 0] << 16) | (b[..., 1] << 8) | b[..., 2]
+    v = np.stack([(p >> 18) & 0x3F, (p >> 12) & 0x3F, (p >> 6) & 0x3F, p & 0x3F], axis=-1)
+    return (((v & 0x20) << 2) | (v & 0x1F)).astype(np.uint8).reshape(packed.shape[0], n)
 
 
 def exp_cw(x: float) -> float:

@@ -155,3 +155,20 @@ def test_rms_norm_split_rope_restatement_follows_formula():
     a, b = vh[:, :, :, 0:1, :], vh[:, :, :, 1:2, :]
     ref = np.concatenate([a * c - b * s, b * c + a * s], axis=3).reshape(B, S, H)
     assert _rel(_f64(out), ref) < BF16_REL
+
+
+def test_fp6_pack_roundtrip_and_layout():
+    """Pack layout of fp6_pack.cu:8-41 on a hand-checked group, and the round trip of
+    FP6-range codes (top two exponent bits zero)."""
+    c = np.array([[0x9F, 0x01, 0x15, 0x80, 0x00, 0x1F, 0x8A, 0x11]], np.uint8)
+    v = [0x3F, 0x01, 0x15, 0x20, 0x00, 0x1F, 0x2A, 0x11]           # s -> bit 5, bits 4..0 kept
+    p0 = v[0] << 18 | v[1] << 12 | v[2] << 6 | v[3]
+    p1 = v[4] << 18 | v[5] << 12 | v[6] << 6 | v[7]
+    expect = [p0 >> 16, (p0 >> 8) & 0xFF, p0 & 0xFF, p1 >> 16, (p1 >> 8) & 0xFF, p1 & 0xFF]
+    assert O.fp6_pack(c).tolist() == [expect]
+    g = np.random.default_rng(0)
+    codes = g.integers(0, 256, (16, 256), dtype=np.uint8) & 0x9F   # FP6-range codes
+    assert np.array_equal(O.fp6_unpack(O.fp6_pack(codes), 256), codes)
+    w = np.random.default_rng(1).normal(0, 0.02, (128, 256)).astype(np.float32)
+    q, s = O.quant_weight_128x128(w, 0.1172)
+    assert ((q & 0x60) == 0).all()                                 # the FP6 quantiser never sets them
