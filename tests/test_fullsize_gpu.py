@@ -1,0 +1,124 @@
+"""Parity at BASELINE.json's full sizes, checked on sampled rows and by size-independent
+properties (the oracle finishes a full-size GEMM row block in well under a second;
+the whole product would take minutes on the CPU).
+
+* config 1: the DiT FFN pair at 24576 tokens (4096 -> 16384 with GELU + requant ->
+  16384 -> 4096), sampled rows against the dequantise-then-fp32 oracle; the fused
+  requant codes bit-exact against quantising the kernel's own bf16 output.
+* the 1x128 quantiser on the down projection's input size (24576 x 16384), sampled
+  rows bit-exact.
+* config 3 shapes with split-K (audio / text token counts) on sampled rows.
+* determinism and row independence at full size.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import activations, bias as make_bias, bits, scales_mn, weights
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_FRO = 1e-2
+MAX_ABS_NORM = 2e-2
+
+
+def _rows(M, n=48, seed=0):
+    g = np.random.default_rng(seed)
+    pick = g.choice(M, size=n, replace=False)
+    edge = np.array([0, 1, 127, 128, M - 129, M - 1])  # tile edges
+    return np.unique(np.concatenate([pick, edge[(edge >= 0) & (edge < M)]]))
+
+
+def _check(out_rows_bf16, ref):
+    m = O.error_metrics(O.bf16_to_f32(out_rows_bf16), ref)
+    assert m["rel_fro"] <= REL_FRO and m["max_abs_norm"] <= MAX_ABS_NORM, m
+    return m
+
+
+def _big_activations(M, K, seed, dev):
+    """BASELINE activations (N(0,1), 1 % channels x20) generated on the device."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, generator=g, device=dev)
+    ch = torch.randperm(K, generator=g, device=dev)[: max(1, K // 100)]
+    x[:, ch] *= 20.0
+    return x.to(torch.bfloat16)
+
+
+def test_ffn_pair_config1_sampled_rows(cuda_device):
+    from ltx_kernels.blockwise import ops
+    M, D, F = 24576, 4096, 16384
+    x = _big_activations(M, D, 1, cuda_device)
+    w1, w2 = weights(F, D, seed=2), weights(D, F, seed=3)
+    b1, b2 = make_bias(F, seed=4), make_bias(D, seed=5)
+    w1q, w1s = ops.quantize_weight_128x128(w1.to(cuda_device))
+    w2q, w2s = ops.quantize_weight_128x128(w2.to(cuda_device))
+    aq, asc = ops.quantize_1x128(x)
+    h, hq, hs = ops.gemm(aq, asc, w1q, w1s, b1.to(cuda_device), gelu=True, requant=True, write_d=True)
+    y = ops.gemm(hq, hs, w2q, w2s, b2.to(cuda_device))
+    torch.cuda.synchronize()
+    rows = _rows(M, seed=7)
+    ri = torch.from_numpy(rows).to(cuda_device)
+    aq_r, asc_r = bits(aq[ri]), scales_mn(asc, M)[:, rows]
+    w1q_b, w1s_n = bits(w1q), w1s.cpu().numpy()
+    # up projection: bf16(GELU(bf16(acc + bias))) against the oracle, rows sampled
+    up_ref = O.gemm_dequant_f32(aq_r, asc_r, w1q_b, w1s_n, b1.numpy())
+    gelu_ref = O.bf16_to_f32(O.gelu_tanh_bf16(O.f32_to_bf16(up_ref)))
+    _check(bits(h[ri]), gelu_ref)
+    # the fused requant equals quantising the kernel's own bf16 output
+    oq, os_ = O.quant_act_1x128(bits(h[ri]))
+    assert O.codes_equal(bits(hq[ri]), oq).all()
+    assert O.scales_equal(scales_mn(hs, M)[:, rows], os_[:, : len(rows)]).all()
+    # down projection from the requantised hidden state
+    down_ref = O.gemm_dequant_f32(bits(hq[ri]), scales_mn(hs, M)[:, rows], bits(w2q), w2s.cpu().numpy(), b2.numpy())
+    _check(bits(y[ri]), down_ref)
+    # determinism at full size
+    y2 = ops.gemm(hq, hs, w2q, w2s, b2.to(cuda_device))
+    assert torch.equal(y, y2)
+
+
+def test_quant_full_size_sampled_rows(cuda_device):
+    from ltx_kernels.blockwise import ops
+    M, K = 24576, 16384
+    x = _big_activations(M, K, 11, cuda_device)
+    q, s = ops.quantize_1x128(x)
+    torch.cuda.synchronize()
+    rows = _rows(M, n=64, seed=12)
+    ri = torch.from_numpy(rows).to(cuda_device)
+    oq, os_ = O.quant_act_1x128(bits(x[ri]))
+    assert O.codes_equal(bits(q[ri]), oq).all()
+    assert O.scales_equal(scales_mn(s, M)[:, rows], os_[:, : len(rows)]).all()
+    # decode -> close to the input (round trip of the 1x128 format)
+    deq = ops.dequantize_1x128(q[ri].contiguous(), s[ri])
+    rel = ((deq.float() - x[ri].float()).norm() / x[ri].float().norm()).item()
+    assert rel < 0.05
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1024, 2048, 2048),    # audio tokens of one denoising step (CFG 2 x 512), split-K
+    (2048, 4096, 4096),    # text context rows through a 4096 projection
+    (128, 8192, 2048),     # audio FFN up at 8 GPUs (128 rows per rank)
+    (49152, 2048, 4096),   # video -> audio cross-attention projection, full video tokens
+])
+def test_dit_config3_shapes_sampled(cuda_device, M, N, K):
+    from ltx_kernels.blockwise import ops
+    x = _big_activations(M, K, M + N, cuda_device)
+    w = weights(N, K, seed=K + 1)
+    b = make_bias(N, seed=N)
+    wq, ws = ops.quantize_weight_128x128(w.to(cuda_device))
+    aq, asc = ops.quantize_1x128(x)
+    d = ops.gemm(aq, asc, wq, ws, b.to(cuda_device))
+    torch.cuda.synchronize()
+    rows = _rows(M, n=min(48, M), seed=M)
+    ri = torch.from_numpy(rows).to(cuda_device)
+    ref = O.gemm_dequant_f32(bits(aq[ri]), scales_mn(asc, M)[:, rows], bits(wq), ws.cpu().numpy(), b.numpy())
+    _check(bits(d[ri]), ref)
+    # row independence: the rows' results do not depend on the other rows of the batch
+    sub_scales = ops.empty_act_scales(len(rows), K // 128, cuda_device)
+    sub_scales.copy_(asc[ri])
+    d_sub = ops.gemm(aq[ri].contiguous(), sub_scales, wq, ws, b.to(cuda_device), split_k=False)
+    d_full = d[ri]
+    diff = (d_sub.float() - d_full.float()).abs().max().item()
+    assert diff <= 0.02 * d_full.float().abs().max().item()
