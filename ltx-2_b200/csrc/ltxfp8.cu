@@ -25,10 +25,9 @@ using namespace ltxfp8;
 // Split-K scratch of ltxfp8_gemm_static_scratch: a fixed 32 MiB array in the
 // module's global memory, so that entry point needs no allocation.  Every GPU
 // that loads this library's kernels holds it until the process exits.  32 MiB
-// covers the split-K plan of every shape on a 148-SM device: a split is used
-// only while the output has at most sms/2 tiles of 128 x 256, and the plan makes
-// splits x tiles <= sms + tiles - 1, so the fp32 partials take at most
-// (148 + 73) x 128 x 256 x 4 bytes = 27.6 MiB.
+// covers the split-K plan of every shape on a 148-SM device: each split unit
+// keeps a 128 x 256 fp32 block (128 KiB) and the split units of a launch fit in
+// one wave (at most sms = 148 units, 18.5 MiB).
 constexpr size_t kStaticScratchBytes = 32ull << 20;
 static __device__ __align__(256) float g_gemm_static_scratch[kStaticScratchBytes / sizeof(float)];
 
@@ -145,7 +144,7 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
                 const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
   int rc = gemm_prepare<kGelu, kRequant>(d);
   if (rc) return rc;
-  const int units = p.total_tiles * p.k_splits;
+  const int units = p.split_tile0 + (p.total_tiles - p.split_tile0) * p.k_splits;
   const int grid = units < d->sms ? units : d->sms;
   fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, p);
   cudaError_t e = cudaGetLastError();
@@ -154,23 +153,64 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
 }
 
 
-// Split-K plan for the one-CTA kernel: enough work units to cover the SMs,
-// at least two K blocks per unit, at most 16 units per tile.
-int splitk_plan(const DeviceInfo* d, int64_t total_tiles, int64_t num_kb, int* kb_per_split) {
-  *kb_per_split = static_cast<int>(num_kb);
-  if (total_tiles * 2 > d->sms || num_kb < 4) return 1;
-  int64_t want = (d->sms + total_tiles - 1) / total_tiles;
-  if (want > num_kb / 2) want = num_kb / 2;
-  if (want > 16) want = 16;
-  if (want < 2) return 1;
-  const int64_t kbps = (num_kb + want - 1) / want;
-  *kb_per_split = static_cast<int>(kbps);
-  return static_cast<int>((num_kb + kbps - 1) / kbps);
+// Split-K plan for the one-CTA kernel.  Candidates: skinny outputs (at most
+// sms/2 tiles) split every tile; larger ones split only the tiles of a last wave
+// that would leave more than half the SMs idle.  The split units must fit in one
+// wave (tiles x splits <= sms), keep at least two K blocks each, and at most 16
+// splits.  A simple cost model picks the split count, in units of one K block of
+// one tile (~0.5 us): the split wave costs ceil(kb / splits) blocks, plus about 6
+// for the reduction launch, plus the fp32 partials written and read back (128 KiB
+// per unit, ~0.1 block per unit at the copy bandwidth); the unsplit wave costs kb.
+// Splitting happens only when it is cheaper.
+struct SplitPlan {
+  int split_tile0, splits, kb_per_split;
+};
+
+SplitPlan splitk_plan(const DeviceInfo* d, int64_t total_tiles, int64_t num_kb) {
+  SplitPlan pl{static_cast<int>(total_tiles), 1, static_cast<int>(num_kb)};
+  if (num_kb < 4) return pl;
+  int64_t split_tiles = 0;
+  if (total_tiles * 2 <= d->sms) {
+    split_tiles = total_tiles;
+  } else if (total_tiles > d->sms) {
+    // A sparse last wave runs at a higher clock under the power cap, so only long
+    // tiles (K >= 8192) gain from splitting it (measured: +11 % at K = 16384,
+    // +3 % at K = 8192, -4 % at K = 4096).
+    const int64_t tail = total_tiles % d->sms;
+    if (tail == 0 || tail * 2 > d->sms || num_kb < 64) return pl;
+    split_tiles = tail;
+  } else {
+    return pl;
+  }
+  int64_t max_s = d->sms / split_tiles;
+  if (max_s > num_kb / 2) max_s = num_kb / 2;
+  if (max_s > 16) max_s = 16;
+  double best = static_cast<double>(num_kb);
+  int64_t best_s = 1;
+  for (int64_t sp = 2; sp <= max_s; ++sp) {
+    const int64_t kbps = (num_kb + sp - 1) / sp;
+    const double cost = static_cast<double>(kbps) + 6.0 + 0.105 * static_cast<double>(split_tiles * sp);
+    if (cost < best) {
+      best = cost;
+      best_s = sp;
+    }
+  }
+  if (best_s < 2) return pl;
+  const int64_t kbps = (num_kb + best_s - 1) / best_s;
+  pl.split_tile0 = static_cast<int>(total_tiles - split_tiles);
+  pl.kb_per_split = static_cast<int>(kbps);
+  pl.splits = static_cast<int>((num_kb + kbps - 1) / kbps);
+  return pl;
+}
+
+size_t splitk_bytes(int64_t total_tiles, const SplitPlan& pl) {
+  if (pl.splits < 2) return 0;
+  return static_cast<size_t>(total_tiles - pl.split_tile0) * static_cast<size_t>(pl.splits) * kBM * kBN * 4u;
 }
 
 template <bool kGelu, bool kRequant>
 int splitk_reduce_launch(const DeviceInfo* d, const GemmParams& p, cudaStream_t stream) {
-  const int64_t groups = static_cast<int64_t>(p.M) * (p.N / 128);
+  const int64_t groups = static_cast<int64_t>(p.total_tiles - p.split_tile0) * kBM * 2;
   const unsigned blocks = static_cast<unsigned>((groups + 15) / 16);
   splitk_reduce_kernel<kGelu, kRequant><<<blocks, 256, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
@@ -183,7 +223,7 @@ template <bool kGelu, bool kRequant>
 int gemm_launch_full(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
                      const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
   int rc = gemm_launch<kGelu, kRequant>(d, a, b, lx, lb, p, stream);
-  if (rc || p.k_splits == 1) return rc;
+  if (rc || p.split_tile0 >= p.total_tiles) return rc;
   return splitk_reduce_launch<kGelu, kRequant>(d, p, stream);
 }
 
@@ -777,15 +817,16 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0);
   p.k_splits = 1;
   p.kb_per_split = p.num_kb;
+  p.split_tile0 = p.total_tiles;
   p.ws = nullptr;
   if (!use_pair && e.workspace) {
-    int kbps = p.num_kb;
-    const int splits = splitk_plan(d, p.total_tiles, p.num_kb, &kbps);
-    const size_t need = static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4u;
-    if (splits > 1 && need <= e.workspace_bytes) {
+    const SplitPlan pl = splitk_plan(d, p.total_tiles, p.num_kb);
+    const size_t need = splitk_bytes(p.total_tiles, pl);
+    if (need > 0 && need <= e.workspace_bytes) {
       if (!aligned(e.workspace, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: workspace must be 16-byte aligned");
-      p.k_splits = splits;
-      p.kb_per_split = kbps;
+      p.k_splits = pl.splits;
+      p.kb_per_split = pl.kb_per_split;
+      p.split_tile0 = pl.split_tile0;
       p.ws = static_cast<float*>(e.workspace);
     }
   }
@@ -813,9 +854,7 @@ int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) 
   int rc = device_info(&d);
   if (rc) return rc;
   const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  int kbps = 0;
-  const int splits = splitk_plan(d, tiles, K / kBK, &kbps);
-  if (splits > 1) *bytes = static_cast<size_t>(splits) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4u;
+  *bytes = splitk_bytes(tiles, splitk_plan(d, tiles, K / kBK));
   return LTXFP8_OK;
 }
 
