@@ -319,10 +319,10 @@ def build_dit_step(dev, world: int, rank: int, scaling: str, blocks: int = DIT_B
     flops *= blocks
     desc = (f"DiT linear stack (BASELINE config 3): {blocks} blocks x 28 FP8 GEMMs, CFG batch 2, tokens per rank "
             f"video {toks['video']} / audio {toks['audio']} / text {toks['text']} ({scaling} scaling)")
-    # kernels per step: one GEMM each, plus the split-K reduction where the shape splits
+    # kernels per step: each GEMM's launches (split-K GEMM and reduction where the shape splits)
     launches = 0
     for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
-        launches += 1 + (1 if ops.gemm_workspace_bytes(toks[cls], N, K, dev) > 0 else 0)
+        launches += ops.gemm_plan(toks[cls], N, K, dev)["launches"]
     launches *= blocks
     return step, flops, launches, desc, toks
 
@@ -925,8 +925,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": M * out_dim * 2},
-            "gpu_launches": args.steps * ((n_ev - 1) + sum(1 for K, N, _ in layers
-                                                           if ops.gemm_workspace_bytes(M, N, K, dev) > 0)),
+            "gpu_launches": args.steps * ((n_ev - 1) + sum(ops.gemm_plan(M, N, K, dev)["launches"] - 1
+                                                           for K, N, _ in layers)),
             "clocks": clk,
         }
         print(json.dumps(out))

@@ -222,12 +222,25 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
 
 /*
  * Scratch bytes ltxfp8_gemm would use for split-K at this shape on the current
- * device (0 when the shape has enough output tiles to fill the GPU without it).
- * Skinny GEMMs (few 128 x 256 output tiles) divide each tile's K blocks among
- * several CTAs, write fp32 partials to the workspace and reduce them in a fixed
- * order (deterministic).  No reference counterpart (the SM89 kernel has no split-K).
+ * device (0 when it splits nothing).  Skinny GEMMs (few 128 x 256 output tiles)
+ * divide each tile's K blocks among several CTAs, write fp32 partials to the
+ * workspace and reduce them in a fixed order (deterministic); for K >= 8192 a
+ * mostly empty last wave of output tiles is split the same way (its rows as a
+ * second, skinny launch).  No reference counterpart (the SM89 kernel has no
+ * split-K).
  */
 int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes);
+
+/* How ltxfp8_gemm launches a shape on the current device when given the workspace. */
+typedef struct ltxfp8_gemm_plan_info {
+  size_t workspace_bytes; /* = ltxfp8_gemm_workspace_bytes */
+  int launches;           /* kernel launches of one call (GEMMs and the split-K reduction) */
+  int splits;             /* K splits of the split rows; 1: no split */
+  int64_t split_row0;     /* rows [0, split_row0) unsplit, [split_row0, M) split; M: no split */
+} ltxfp8_gemm_plan_info;
+
+/* Fills *info for an M x N x K GEMM (no reference counterpart). */
+int ltxfp8_gemm_plan(int64_t M, int64_t N, int64_t K, ltxfp8_gemm_plan_info* info);
 
 /*
  * ltxfp8_gemm for callers that cannot allocate device memory per call: a host

@@ -79,22 +79,15 @@ struct GemmParams {
   int64_t s_out_ld;
   float lora_alpha;
   int flags;
-  // Split-K: the tiles from split_tile0 on have their K blocks divided among
-  // k_splits work units (all tiles for skinny M; the tiles of a mostly empty last
-  // wave otherwise).  Unit partials (fp32, no bias) go to a compact workspace,
-  // one 128 x 256 block per (split tile, split) at
-  // ws[((tile - split_tile0) * k_splits + split) * 128 * 256], and
-  // splitk_reduce_kernel sums them in split order.  split_tile0 == total_tiles
-  // (k_splits = 1): no split.
+  // Split-K for skinny M: each output tile's K blocks are divided among k_splits
+  // work units; unit u = tile * k_splits + split writes its fp32 partial (no
+  // bias) to the 128 x 256 workspace block ws[u * 128 * 256], and
+  // splitk_reduce_kernel sums a tile's partials in split order.  k_splits = 1:
+  // no split.
   int k_splits;
   int kb_per_split;
-  int split_tile0;
   float* ws;
 };
-
-__device__ __forceinline__ int gemm_total_units(const GemmParams& p) {
-  return p.split_tile0 + (p.total_tiles - p.split_tile0) * p.k_splits;
-}
 
 // Grouped rasterisation: consecutive tile indices walk group_m M-tiles down a
 // column of N-tiles, so the CTAs resident at one time share A and W tiles in L2.
@@ -112,27 +105,16 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, const GemmParams& p, 
 // whole range unless split-K is on); LoRA blocks ride with the last split.
 struct GemmUnit {
   int mt, nt, split, kb_begin, n_fp8, n_blocks;
-  int slot;  // -1: whole tile; else the unit's 128 x 256 partial block in the workspace
 };
 
 __device__ __forceinline__ GemmUnit gemm_unit(int u, const GemmParams& p) {
   GemmUnit w;
-  if (u < p.split_tile0) {
-    gemm_tile_coords(u, p, w.mt, w.nt);
-    w.split = 0;
-    w.kb_begin = 0;
-    w.n_fp8 = p.num_kb;
-    w.n_blocks = p.num_kb + p.num_lora;
-    w.slot = -1;
-    return w;
-  }
-  const int st = (u - p.split_tile0) / p.k_splits;
-  w.split = (u - p.split_tile0) - st * p.k_splits;
-  gemm_tile_coords(p.split_tile0 + st, p, w.mt, w.nt);
+  const int tile = u / p.k_splits;
+  w.split = u - tile * p.k_splits;
+  gemm_tile_coords(tile, p, w.mt, w.nt);
   w.kb_begin = w.split * p.kb_per_split;
   w.n_fp8 = min(p.kb_per_split, p.num_kb - w.kb_begin);
   w.n_blocks = w.n_fp8 + (w.split == p.k_splits - 1 ? p.num_lora : 0);
-  w.slot = st * p.k_splits + w.split;
   return w;
 }
 
@@ -225,7 +207,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // ------------------------------------------------------------ TMA producer
       uint32_t it = 0;
       bool ok = true;
-      const int total_units = gemm_total_units(p);
+      const int total_units = p.total_tiles * p.k_splits;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         const GemmUnit w = gemm_unit(u, p);
         const int m0 = w.mt * kBM, n0 = w.nt * kBN;
@@ -259,7 +241,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t kIdescBF16 = make_idesc(1u, kBM, kBN);
       uint32_t it = 0;
       bool ok = true;
-      const int total_units = gemm_total_units(p);
+      const int total_units = p.total_tiles * p.k_splits;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         const GemmUnit w = gemm_unit(u, p);
         for (int kb = 0; kb < w.n_blocks; ++kb, ++it) {
@@ -303,7 +285,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 4) >> 2; // which 128-column half of the 256-wide tile
     uint32_t it = 0;
     bool ok = true;
-    const int total_units = gemm_total_units(p);
+    const int total_units = p.total_tiles * p.k_splits;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       const GemmUnit w = gemm_unit(u, p);
       const int row = w.mt * kBM + sp * 32 + lane;
@@ -344,9 +326,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok) break;
       if (!(row_ok && col_ok)) continue;
-      if (w.slot >= 0) {
+      if (p.k_splits > 1) {
         // Split-K unit: the raw fp32 partial (no bias) for the reduction kernel.
-        float4* dst = reinterpret_cast<float4*>(p.ws + (static_cast<int64_t>(w.slot) * kBM + sp * 32 + lane) * kBN +
+        float4* dst = reinterpret_cast<float4*>(p.ws + (static_cast<int64_t>(u) * kBM + sp * 32 + lane) * kBN +
                                                 half * 128);
 #pragma unroll
         for (int c = 0; c < 32; ++c) dst[c] = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
@@ -420,20 +402,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// Split-K reduction over the split tiles: out = epilogue( sum_split partial +
-// bias ), summing the unit partials in split order (deterministic).  One
-// half-warp per (tile row, 128-column group): 16 lanes x 8 columns, so the 1x128
-// requantisation needs no cross-row reduction.  Epilogue semantics are those of
-// the GEMM kernel.
+// Split-K reduction: out = epilogue( sum_split partial + bias ), summing each
+// tile's unit partials in split order (deterministic).  One half-warp per (tile
+// row, 128-column group): 16 lanes x 8 columns, so the 1x128 requantisation needs
+// no cross-row reduction.  Epilogue semantics are those of the GEMM kernel.
 template <bool kGelu, bool kRequant>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmParams p) {
-  const int64_t total = static_cast<int64_t>(p.total_tiles - p.split_tile0) * kBM * 2;
+  const int64_t total = static_cast<int64_t>(p.total_tiles) * kBM * 2;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);
   const int l16 = threadIdx.x & 15;
   const int st = static_cast<int>(gid / (kBM * 2));
   const int r = static_cast<int>((gid >> 1) % kBM), g = static_cast<int>(gid & 1);
   int mt = 0, nt = 0;
-  if (gid < total) gemm_tile_coords(p.split_tile0 + st, p, mt, nt);
+  if (gid < total) gemm_tile_coords(st, p, mt, nt);
   const int row = mt * kBM + r;
   const int col = nt * kBN + g * 128 + l16 * 8;
   const int grp = col / 128;

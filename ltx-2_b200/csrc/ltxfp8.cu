@@ -144,7 +144,7 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
                 const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
   int rc = gemm_prepare<kGelu, kRequant>(d);
   if (rc) return rc;
-  const int units = p.split_tile0 + (p.total_tiles - p.split_tile0) * p.k_splits;
+  const int units = p.total_tiles * p.k_splits;
   const int grid = units < d->sms ? units : d->sms;
   fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, p);
   cudaError_t e = cudaGetLastError();
@@ -153,43 +153,28 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
 }
 
 
-// Split-K plan for the one-CTA kernel.  Candidates: skinny outputs (at most
-// sms/2 tiles) split every tile; larger ones split only the tiles of a last wave
-// that would leave more than half the SMs idle.  The split units must fit in one
-// wave (tiles x splits <= sms), keep at least two K blocks each, and at most 16
-// splits.  A simple cost model picks the split count, in units of one K block of
-// one tile (~0.5 us): the split wave costs ceil(kb / splits) blocks, plus about 6
-// for the reduction launch, plus the fp32 partials written and read back (128 KiB
-// per unit, ~0.1 block per unit at the copy bandwidth); the unsplit wave costs kb.
-// Splitting happens only when it is cheaper.
+// Split-K plan for a skinny launch of the one-CTA kernel (at most sms/2 tiles of
+// 128 x 256): every tile's K blocks are divided into S units of at least two
+// blocks, at most 16, all units in one wave (tiles x S <= sms).  A cost model in
+// units of one K block of one tile (~0.5 us) picks S and skips splits that do not
+// pay: the split wave costs ceil(kb / S), plus ~6 for the reduction launch, plus
+// ~0.1 per unit for the fp32 partials written and read back (128 KiB each); the
+// unsplit wave costs kb.
 struct SplitPlan {
-  int split_tile0, splits, kb_per_split;
+  int splits, kb_per_split;
 };
 
 SplitPlan splitk_plan(const DeviceInfo* d, int64_t total_tiles, int64_t num_kb) {
-  SplitPlan pl{static_cast<int>(total_tiles), 1, static_cast<int>(num_kb)};
-  if (num_kb < 4) return pl;
-  int64_t split_tiles = 0;
-  if (total_tiles * 2 <= d->sms) {
-    split_tiles = total_tiles;
-  } else if (total_tiles > d->sms) {
-    // A sparse last wave runs at a higher clock under the power cap, so only long
-    // tiles (K >= 8192) gain from splitting it (measured: +11 % at K = 16384,
-    // +3 % at K = 8192, -4 % at K = 4096).
-    const int64_t tail = total_tiles % d->sms;
-    if (tail == 0 || tail * 2 > d->sms || num_kb < 64) return pl;
-    split_tiles = tail;
-  } else {
-    return pl;
-  }
-  int64_t max_s = d->sms / split_tiles;
+  SplitPlan pl{1, static_cast<int>(num_kb)};
+  if (num_kb < 4 || total_tiles * 2 > d->sms) return pl;
+  int64_t max_s = d->sms / total_tiles;
   if (max_s > num_kb / 2) max_s = num_kb / 2;
   if (max_s > 16) max_s = 16;
   double best = static_cast<double>(num_kb);
   int64_t best_s = 1;
   for (int64_t sp = 2; sp <= max_s; ++sp) {
     const int64_t kbps = (num_kb + sp - 1) / sp;
-    const double cost = static_cast<double>(kbps) + 6.0 + 0.105 * static_cast<double>(split_tiles * sp);
+    const double cost = static_cast<double>(kbps) + 6.0 + 0.105 * static_cast<double>(total_tiles * sp);
     if (cost < best) {
       best = cost;
       best_s = sp;
@@ -197,20 +182,62 @@ SplitPlan splitk_plan(const DeviceInfo* d, int64_t total_tiles, int64_t num_kb) 
   }
   if (best_s < 2) return pl;
   const int64_t kbps = (num_kb + best_s - 1) / best_s;
-  pl.split_tile0 = static_cast<int>(total_tiles - split_tiles);
   pl.kb_per_split = static_cast<int>(kbps);
   pl.splits = static_cast<int>((num_kb + kbps - 1) / kbps);
   return pl;
 }
 
-size_t splitk_bytes(int64_t total_tiles, const SplitPlan& pl) {
-  if (pl.splits < 2) return 0;
-  return static_cast<size_t>(total_tiles - pl.split_tile0) * static_cast<size_t>(pl.splits) * kBM * kBN * 4u;
+// How one ltxfp8_gemm call is launched: output rows [0, split_row0) as one
+// unsplit GEMM, rows [split_row0, M) as a split-K GEMM (plus its reduction).
+//  * skinny outputs (at most sms/2 tiles): split_row0 = 0, every tile split;
+//  * outputs whose last wave of tiles would leave more than half the SMs idle,
+//    for K >= 8192: the last M-tile rows that cover that wave become their own
+//    skinny split-K launch, the rest fills whole waves.  (A sparse last wave runs
+//    at a higher clock under the power cap, so short tiles do not gain: measured
+//    +11 % at K = 16384, +3 % at K = 8192, -4 % at K = 4096 when the same split
+//    ran inside one launch.)
+//  * otherwise split_row0 = M: one unsplit launch.
+constexpr int64_t kTailSplitMinKb = 64;
+
+struct GemmPlan {
+  int64_t split_row0;
+  int64_t split_tiles;  // output tiles of the split rows
+  SplitPlan split;      // split.splits == 1: no split launch
+};
+
+GemmPlan gemm_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K) {
+  const int64_t m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + kBN - 1) / kBN;
+  const int64_t tiles = m_tiles * n_tiles, num_kb = K / kBK;
+  GemmPlan g{M, 0, SplitPlan{1, static_cast<int>(num_kb)}};
+  if (tiles * 2 <= d->sms) {
+    const SplitPlan sp = splitk_plan(d, tiles, num_kb);
+    if (sp.splits > 1) g = GemmPlan{0, tiles, sp};
+    return g;
+  }
+  const int64_t rem = tiles % d->sms;
+  if (num_kb < kTailSplitMinKb || rem == 0 || rem * 2 > d->sms) return g;
+  const int64_t tail_m_tiles = (rem + n_tiles - 1) / n_tiles;
+  const int64_t tail_tiles = tail_m_tiles * n_tiles;
+  if (tail_m_tiles >= m_tiles || tail_tiles * 2 > d->sms) return g;
+  const SplitPlan sp = splitk_plan(d, tail_tiles, num_kb);
+  if (sp.splits > 1) g = GemmPlan{(m_tiles - tail_m_tiles) * kBM, tail_tiles, sp};
+  return g;
+}
+
+size_t splitk_bytes(const GemmPlan& g) {
+  if (g.split.splits < 2) return 0;
+  return static_cast<size_t>(g.split_tiles) * static_cast<size_t>(g.split.splits) * kBM * kBN * 4u;
+}
+
+// Kernel launches of one call: the unsplit GEMM, the split GEMM, its reduction.
+int gemm_plan_launches(const GemmPlan& g) {
+  if (g.split.splits < 2) return 1;
+  return (g.split_row0 > 0 ? 1 : 0) + 2;
 }
 
 template <bool kGelu, bool kRequant>
 int splitk_reduce_launch(const DeviceInfo* d, const GemmParams& p, cudaStream_t stream) {
-  const int64_t groups = static_cast<int64_t>(p.total_tiles - p.split_tile0) * kBM * 2;
+  const int64_t groups = static_cast<int64_t>(p.total_tiles) * kBM * 2;
   const unsigned blocks = static_cast<unsigned>((groups + 15) / 16);
   splitk_reduce_kernel<kGelu, kRequant><<<blocks, 256, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
@@ -223,7 +250,7 @@ template <bool kGelu, bool kRequant>
 int gemm_launch_full(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
                      const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
   int rc = gemm_launch<kGelu, kRequant>(d, a, b, lx, lb, p, stream);
-  if (rc || p.split_tile0 >= p.total_tiles) return rc;
+  if (rc || p.k_splits == 1) return rc;
   return splitk_reduce_launch<kGelu, kRequant>(d, p, stream);
 }
 
@@ -728,6 +755,88 @@ int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld
   return LTXFP8_OK;
 }
 
+// One launch (plus its split-K reduction) of the GEMM over output rows
+// [row0, row0 + rows): the operands and outputs of those rows are addressed by
+// offsetting A, sfa, D, the requant outputs and the LoRA rows; N, K, W, sfb and
+// the bias are shared.  split != nullptr: split-K with that plan, partials in
+// the caller's workspace.
+static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                     const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue& e,
+                     int64_t row0, int64_t rows, const SplitPlan* split, bool use_pair, cudaStream_t stream) {
+  const bool write_d = !e.skip_d;
+  const bool lora = e.lora_ax != nullptr;
+  const int tile_m = use_pair ? pair::kTileM : kBM;
+  const int tile_n = use_pair ? pair::kTileN : kBN;
+  const uint32_t w_rows_per_load = use_pair ? pair::kRowsPerCta : kBN;  // W rows each CTA loads
+  const auto* a_rows = static_cast<const uint8_t*>(A) + row0 * K;
+
+  CUtensorMap ma, mb, mlx, mlb;
+  int rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_rows, K, rows, K, kBK, kBM);
+  if (rc) return rc;
+  rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, w_rows_per_load);
+  if (rc) return rc;
+  if (lora) {
+    const auto* lx_rows = static_cast<const __nv_bfloat16*>(e.lora_ax) + row0 * e.lora_r;
+    rc = make_map_2d(&mlx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lx_rows, e.lora_r, rows, e.lora_r * 2, kLoraChunk, kBM);
+    if (rc) return rc;
+    rc = make_map_2d(&mlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_b, e.lora_r, N, e.lora_r * 2, kLoraChunk,
+                     w_rows_per_load);
+    if (rc) return rc;
+  } else {
+    mlx = ma;  // unused
+    mlb = mb;
+  }
+
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(rows);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.num_kb = static_cast<int>(K / kBK);
+  p.num_lora = lora ? static_cast<int>((e.lora_r + kLoraChunk - 1) / kLoraChunk) : 0;
+  p.m_tiles = static_cast<int>((rows + tile_m - 1) / tile_m);
+  p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
+  // Rasterisation for L2 reuse: group enough M tiles that one group's A slab is
+  // ~24 MB and sweep the N tiles within the group, so the CTAs resident at one
+  // time share A and W tiles through L2.  (Walking N fastest to keep a whole
+  // <= 67 MB weight resident measured worse: the weight does not stay in L2.)
+  int64_t gm = (24ll << 20) / (static_cast<int64_t>(tile_m) * K);
+  if (gm < 1) gm = 1;
+  if (gm > p.m_tiles) gm = p.m_tiles;
+  p.group_m = static_cast<int>(gm);
+  p.total_tiles = p.m_tiles * p.n_tiles;
+  p.sfa = sfa + row0;
+  p.sfa_ld = sfa_ld;
+  p.sfb = sfb;
+  p.bias = bias;
+  p.d = write_d ? static_cast<__nv_bfloat16*>(D) + row0 * N : nullptr;
+  p.q_out = e.requant_q ? static_cast<uint8_t*>(e.requant_q) + row0 * N : nullptr;
+  p.s_out = e.requant_scales ? e.requant_scales + row0 : nullptr;
+  p.s_out_ld = e.requant_ld;
+  p.lora_alpha = e.lora_alpha;
+  p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0);
+  p.k_splits = 1;
+  p.kb_per_split = p.num_kb;
+  p.ws = nullptr;
+  if (split) {
+    p.k_splits = split->splits;
+    p.kb_per_split = split->kb_per_split;
+    p.ws = static_cast<float*>(e.workspace);
+  }
+
+  const bool gelu = e.gelu_tanh != 0, requant = e.requant_q != nullptr;
+  if (use_pair) {
+    if (gelu && requant) return gemm_pair_launch<true, true>(d, ma, mb, mlx, mlb, p, stream);
+    if (gelu) return gemm_pair_launch<true, false>(d, ma, mb, mlx, mlb, p, stream);
+    if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, p, stream);
+    return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, p, stream);
+  }
+  if (gelu && requant) return gemm_launch_full<true, true>(d, ma, mb, mlx, mlb, p, stream);
+  if (gelu) return gemm_launch_full<true, false>(d, ma, mb, mlx, mlb, p, stream);
+  if (requant) return gemm_launch_full<false, true>(d, ma, mb, mlx, mlb, p, stream);
+  return gemm_launch_full<false, false>(d, ma, mb, mlx, mlb, p, stream);
+}
+
 int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
                 const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
                 void* stream) {
@@ -765,84 +874,19 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   // Default: the one-CTA kernel.  The CTA-pair kernel (256-row tiles over two
   // SMs) is selected explicitly; it halves the W bytes each SM streams but is
   // not yet faster on the FFN shapes.
-  const int variant = g_gemm_variant.load();
-  const bool use_pair = variant == 2;
-  const int tile_m = use_pair ? pair::kTileM : kBM;
-  const int tile_n = use_pair ? pair::kTileN : kBN;
-  const uint32_t w_rows_per_load = use_pair ? pair::kRowsPerCta : kBN;  // W rows each CTA loads
-
-  CUtensorMap ma, mb, mlx, mlb;
-  rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, K, kBK, kBM);
-  if (rc) return rc;
-  rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, w_rows_per_load);
-  if (rc) return rc;
-  if (lora) {
-    rc = make_map_2d(&mlx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_ax, e.lora_r, M, e.lora_r * 2, kLoraChunk, kBM);
-    if (rc) return rc;
-    rc = make_map_2d(&mlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, e.lora_b, e.lora_r, N, e.lora_r * 2, kLoraChunk,
-                     w_rows_per_load);
-    if (rc) return rc;
-  } else {
-    mlx = ma;  // unused
-    mlb = mb;
-  }
-
-  GemmParams p;
-  memset(&p, 0, sizeof(p));
-  p.M = static_cast<int>(M);
-  p.N = static_cast<int>(N);
-  p.K = static_cast<int>(K);
-  p.num_kb = static_cast<int>(K / kBK);
-  p.num_lora = lora ? static_cast<int>((e.lora_r + kLoraChunk - 1) / kLoraChunk) : 0;
-  p.m_tiles = static_cast<int>((M + tile_m - 1) / tile_m);
-  p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
-  // Rasterisation for L2 reuse: group enough M tiles that one group's A slab is
-  // ~24 MB and sweep the N tiles within the group, so the CTAs resident at one
-  // time share A and W tiles through L2.  (Walking N fastest to keep a whole
-  // <= 67 MB weight resident measured worse: the weight does not stay in L2.)
-  int64_t gm = (24ll << 20) / (static_cast<int64_t>(tile_m) * K);
-  if (gm < 1) gm = 1;
-  if (gm > p.m_tiles) gm = p.m_tiles;
-  p.group_m = static_cast<int>(gm);
-  p.total_tiles = p.m_tiles * p.n_tiles;
-  p.sfa = sfa;
-  p.sfa_ld = sfa_ld;
-  p.sfb = sfb;
-  p.bias = bias;
-  p.d = static_cast<__nv_bfloat16*>(D);
-  p.q_out = static_cast<uint8_t*>(e.requant_q);
-  p.s_out = e.requant_scales;
-  p.s_out_ld = e.requant_ld;
-  p.lora_alpha = e.lora_alpha;
-  p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0);
-  p.k_splits = 1;
-  p.kb_per_split = p.num_kb;
-  p.split_tile0 = p.total_tiles;
-  p.ws = nullptr;
-  if (!use_pair && e.workspace) {
-    const SplitPlan pl = splitk_plan(d, p.total_tiles, p.num_kb);
-    const size_t need = splitk_bytes(p.total_tiles, pl);
-    if (need > 0 && need <= e.workspace_bytes) {
-      if (!aligned(e.workspace, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: workspace must be 16-byte aligned");
-      p.k_splits = pl.splits;
-      p.kb_per_split = pl.kb_per_split;
-      p.split_tile0 = pl.split_tile0;
-      p.ws = static_cast<float*>(e.workspace);
-    }
-  }
-
   auto s = static_cast<cudaStream_t>(stream);
-  const bool gelu = e.gelu_tanh != 0, requant = e.requant_q != nullptr;
-  if (use_pair) {
-    if (gelu && requant) return gemm_pair_launch<true, true>(d, ma, mb, mlx, mlb, p, s);
-    if (gelu) return gemm_pair_launch<true, false>(d, ma, mb, mlx, mlb, p, s);
-    if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, p, s);
-    return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, p, s);
+  const bool use_pair = g_gemm_variant.load() == 2;
+  if (use_pair) return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, true, s);
+  const GemmPlan g = gemm_plan(d, M, N, K);
+  const size_t need = splitk_bytes(g);
+  if (need == 0 || !e.workspace || need > e.workspace_bytes)
+    return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, false, s);
+  if (!aligned(e.workspace, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: workspace must be 16-byte aligned");
+  if (g.split_row0 > 0) {
+    rc = gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, g.split_row0, nullptr, false, s);
+    if (rc) return rc;
   }
-  if (gelu && requant) return gemm_launch_full<true, true>(d, ma, mb, mlx, mlb, p, s);
-  if (gelu) return gemm_launch_full<true, false>(d, ma, mb, mlx, mlb, p, s);
-  if (requant) return gemm_launch_full<false, true>(d, ma, mb, mlx, mlb, p, s);
-  return gemm_launch_full<false, false>(d, ma, mb, mlx, mlb, p, s);
+  return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, g.split_row0, M - g.split_row0, &g.split, false, s);
 }
 
 int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) {
@@ -853,8 +897,28 @@ int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) 
   DeviceInfo* d;
   int rc = device_info(&d);
   if (rc) return rc;
-  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  *bytes = splitk_bytes(tiles, splitk_plan(d, tiles, K / kBK));
+  *bytes = splitk_bytes(gemm_plan(d, M, N, K));
+  return LTXFP8_OK;
+}
+
+int ltxfp8_gemm_plan(int64_t M, int64_t N, int64_t K, ltxfp8_gemm_plan_info* info) {
+  if (!info) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm_plan: null pointer");
+  memset(info, 0, sizeof(*info));
+  if (M < 1 || N < 128 || K < 128 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gemm_plan: need M >= 1 and N, K positive multiples of 128");
+  info->launches = 1;
+  info->splits = 1;
+  info->split_row0 = M;
+  if (g_gemm_variant.load() == 2) return LTXFP8_OK;
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const GemmPlan g = gemm_plan(d, M, N, K);
+  if (g.split.splits < 2) return LTXFP8_OK;
+  info->workspace_bytes = splitk_bytes(g);
+  info->launches = gemm_plan_launches(g);
+  info->splits = g.split.splits;
+  info->split_row0 = g.split_row0;
   return LTXFP8_OK;
 }
 

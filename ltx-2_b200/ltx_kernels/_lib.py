@@ -56,6 +56,15 @@ class Epilogue(ctypes.Structure):
     ]
 
 
+class GemmPlanInfo(ctypes.Structure):
+    _fields_ = [
+        ("workspace_bytes", ctypes.c_size_t),
+        ("launches", ctypes.c_int),
+        ("splits", ctypes.c_int),
+        ("split_row0", ctypes.c_int64),
+    ]
+
+
 # name -> (restype, argtypes); the exported symbols of include/ltxfp8.h
 _vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
 SIGNATURES = {
@@ -68,6 +77,7 @@ SIGNATURES = {
     "ltxfp8_lora_a": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ltxfp8_gemm_set_variant": (_i32, [_i32]),
     "ltxfp8_gemm_workspace_bytes": (_i32, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "ltxfp8_gemm_plan": (_i32, [_i64, _i64, _i64, _vp]),
     "ltxfp8_adanorm_quantize": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i32,
                                         _vp]),
     "ltxfp8_rms_fma": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),

@@ -415,6 +415,23 @@ def gemm_workspace_bytes(M: int, N: int, K: int, device) -> int:
     return v
 
 
+_PLAN_CACHE: dict = {}
+
+
+def gemm_plan(M: int, N: int, K: int, device) -> dict:
+    """How ``gemm`` (with split-K allowed) launches this shape: workspace bytes, kernel
+    launches per call, K splits and the first split row (``M``: no split)."""
+    key = (torch.cuda.current_device() if device is None else device.index, M, N, K)
+    v = _PLAN_CACHE.get(key)
+    if v is None:
+        import ctypes
+        info = L.GemmPlanInfo()
+        L.check(L.load().ltxfp8_gemm_plan(M, N, K, ctypes.byref(info)))
+        v = _PLAN_CACHE[key] = {"workspace_bytes": info.workspace_bytes, "launches": info.launches,
+                                "splits": info.splits, "split_row0": info.split_row0}
+    return dict(v)
+
+
 def lora_a(x: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
     """x bf16 [..., K] . A bf16 [r, K]^T -> bf16 [M, r]."""
     _require_cuda("lora_a", x, a)

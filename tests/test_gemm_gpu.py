@@ -351,28 +351,43 @@ def test_splitk_fused_epilogues(cuda_device):
     _check(dl, ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(6144, 4096, 16384), (5120, 4096, 8192), (6144, 8192, 8192)])
+@pytest.mark.parametrize("M,N,K", [(6144, 4096, 16384), (5000, 4096, 8192), (6144, 8192, 8192)])
 def test_tail_wave_split(cuda_device, M, N, K):
     """A mostly empty last wave of long tiles is split along K (the 8-GPU DiT shard sizes):
-    same result as the unsplit kernel up to fp32 summation order, deterministic."""
+    its M-tile rows run as a second, skinny split-K launch.  Same result as the unsplit
+    kernel up to fp32 summation order, deterministic; bias, GELU + requant and LoRA rows
+    addressed correctly on both sides of the split row."""
     from ltx_kernels.blockwise import ops
-    assert ops.gemm_workspace_bytes(M, N, K, cuda_device) > 0
+    plan = ops.gemm_plan(M, N, K, cuda_device)
+    r0 = plan["split_row0"]
+    assert 0 < r0 < M and r0 % 128 == 0 and plan["splits"] > 1 and plan["launches"] == 3, plan
+    assert plan["workspace_bytes"] == ops.gemm_workspace_bytes(M, N, K, cuda_device) > 0
     x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=M + N)
     d = ops.gemm(aq, asc, wq, wsc, b)
     d1 = ops.gemm(aq, asc, wq, wsc, b, split_k=False)
     torch.cuda.synchronize()
-    rows = np.unique(np.concatenate([np.arange(0, M, max(1, M // 40)), [M - 1]]))
+    rows = np.unique(np.concatenate([np.arange(0, M, max(1, M // 40)), [r0 - 1, r0, r0 + 1, M - 1]]))
     ri = torch.from_numpy(rows).to(cuda_device)
     ref = O.gemm_dequant_f32(bits(aq[ri]), scales_mn(asc, M)[:, rows], bits(wq), wsc.cpu().numpy(), b.cpu().numpy())
     m = O.error_metrics(O.bf16_to_f32(bits(d[ri])), ref)
     assert m["rel_fro"] <= REL_FRO and m["max_abs_norm"] <= MAX_ABS_NORM, m
     diff = (d.float() - d1.float()).abs().max().item()
     assert diff <= 0.02 * d1.float().abs().max().item()
+    assert torch.equal(d[:r0], d1[:r0])  # the unsplit rows run the same kernel over the same K order
     assert torch.equal(d, ops.gemm(aq, asc, wq, wsc, b))
-    # fused GELU + requant through the tail reduction
+    # fused GELU + requant through the split rows' reduction
     _, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
     dg = ops.gemm(aq, asc, wq, wsc, b, gelu=True)
     torch.cuda.synchronize()
     oq, os_ = O.quant_act_1x128(bits(dg[ri]))
     assert O.codes_equal(bits(q[ri]), oq).all()
     assert O.scales_equal(scales_mn(s, M)[:, rows], os_[:, : len(rows)]).all()
+    # runtime LoRA: the split rows read their own LoRA rows
+    la, lb = make_lora(N, K, 32, seed=M)
+    ax = ops.lora_a(x.to(cuda_device), la.to(cuda_device))
+    dl = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5)
+    dl1 = ops.gemm(aq, asc, wq, wsc, b, lora_ax=ax, lora_b=lb.to(cuda_device), lora_alpha=0.5, split_k=False)
+    torch.cuda.synchronize()
+    assert torch.equal(dl[:r0], dl1[:r0])
+    diff = (dl.float() - dl1.float()).abs().max().item()
+    assert diff <= 0.02 * dl1.float().abs().max().item()
