@@ -178,6 +178,27 @@ def flops_of(name: str, M: int) -> float:
     return total
 
 
+def build_module(name: str, params, dev):
+    """The workload's layers as the package's public modules, sharing the bench's weights."""
+    from ltx_kernels.blockwise import BlockwiseFP8FeedForward, BlockwiseFP8Linear, BlockwiseFP8LoRALinear
+
+    def linear(K, N, wq, ws, b, lora=None):
+        if lora is None:
+            m = BlockwiseFP8Linear(K, N, bias=True, device=dev)
+        else:
+            la, lb, alpha = lora
+            m = BlockwiseFP8LoRALinear(K, N, la.shape[0], alpha=alpha, bias=True, device=dev)
+            m.lora_A.data, m.lora_B.data = la, lb
+        m.weight.data, m.weight_scale.data, m.bias.data = wq, ws, b
+        return m
+
+    mods = [linear(K, N, wq, ws, b, lora) for (K, N, epi, wq, ws, b, lora) in params]
+    if name == "ffn":
+        return BlockwiseFP8FeedForward.from_linears(mods[0], mods[1])
+    assert len(mods) == 1, name
+    return mods[0]
+
+
 def make_step(x, params):
     """Returns step(events=None) running the workload once on the current stream."""
     import torch
@@ -769,6 +790,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=0, help="tokens per GPU (default: the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=3072,
+                    help="ffn/linear/qkv_lora e2e: tokens per streamed chunk (0: whole batch, copies not overlapped)")
     ap.add_argument("--no-graph", action="store_true", help="dit_step: launch every GEMM from Python instead of "
                                                              "replaying a captured CUDA graph")
     args = ap.parse_args()
@@ -844,18 +867,24 @@ def main():
             per_kernel[j] += evs[i][j].elapsed_time(evs[i][j + 1])
     per_kernel = [t / args.steps for t in per_kernel]
 
-    # ---- end to end through the public API with host buffers
-    from ltx_kernels.blockwise.fused import fp8_linear  # noqa: F401  (public API surface)
+    # ---- end to end through the public API with host buffers: the layer modules
+    # (BlockwiseFP8FeedForward / BlockwiseFP8Linear / BlockwiseFP8LoRALinear) over
+    # pinned host tokens, H2D and D2H inside the timed region, streamed in token
+    # chunks so the copies of neighbouring chunks overlap the GEMMs
+    # (ltx_kernels.blockwise.host_stream); --e2e-chunk 0 copies the whole batch in,
+    # runs the layer and copies it out, one after the other.
+    from ltx_kernels.blockwise.host_stream import TokenStreamer
     x_host = x.cpu().pin_memory()
     out_dim = params[-1][1]
     out_host = torch.empty((M, out_dim), dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, min(args.steps, 10))
+    layer = build_module(args.workload, params, dev)
+    chunk = args.e2e_chunk if args.e2e_chunk > 0 else M
+    streamer = TokenStreamer(layer, x.shape[1], chunk, dev)
 
     def e2e_step():
-        xd = x_host.to(dev, non_blocking=True)
-        sub, _ = make_step(xd, params)
-        out = sub()
-        out_host.copy_(out, non_blocking=True)
+        with torch.inference_mode():
+            streamer(x_host, out_host)
 
     for _ in range(2):
         e2e_step()
@@ -924,7 +953,8 @@ def main():
                          "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": M * out_dim * 2},
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": M * out_dim * 2,
+                    "api": f"{type(layer).__name__} via host_stream.TokenStreamer, {chunk}-token chunks"},
             "gpu_launches": args.steps * ((n_ev - 1) + sum(ops.gemm_plan(M, N, K, dev)["launches"] - 1
                                                            for K, N, _ in layers)),
             "clocks": clk,

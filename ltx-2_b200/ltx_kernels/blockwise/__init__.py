@@ -15,12 +15,14 @@ from ltx_kernels.blockwise.functional import (
 from ltx_kernels.blockwise.linear import BlockwiseFP6Linear, BlockwiseFP8Linear
 from ltx_kernels.blockwise.fused import BlockwiseFP8FeedForward, BlockwiseFP8LoRALinear, fp8_linear
 from ltx_kernels.blockwise.lora_fuse import blockwise_fp8_fuse, blockwise_fp8_fuse_rule, merge_loras
+from ltx_kernels.blockwise.host_stream import TokenStreamer, stream_tokens
 
 __all__ = [
     "BlockwiseFP6Linear",
     "BlockwiseFP8Linear",
     "BlockwiseFP8FeedForward",
     "BlockwiseFP8LoRALinear",
+    "TokenStreamer",
     "blockwise_dequantize",
     "blockwise_fp8_fuse",
     "blockwise_fp8_fuse_rule",
@@ -35,4 +37,5 @@ __all__ = [
     "gated_attention_triton",
     "rms_norm_rope",
     "rms_norm_split_rope",
+    "stream_tokens",
 ]

@@ -1,0 +1,91 @@
+"""Token streaming from host memory (ltx_kernels.blockwise.host_stream): chunked,
+copy-overlapped calls give the whole-batch result row for row."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from inputs import activations, bias as make_bias, lora as make_lora, weights
+
+pytestmark = pytest.mark.gpu
+
+
+def _linear(K, N, dev, seed, lora_rank=0):
+    from ltx_kernels.blockwise import BlockwiseFP8Linear, BlockwiseFP8LoRALinear
+    from ltx_kernels.blockwise import ops
+    if lora_rank:
+        m = BlockwiseFP8LoRALinear(K, N, lora_rank, alpha=0.5, device=dev)
+        la, lb = make_lora(N, K, lora_rank, seed=seed + 7)
+        m.lora_A.data, m.lora_B.data = la.to(dev), lb.to(dev)
+    else:
+        m = BlockwiseFP8Linear(K, N, device=dev)
+    wq, ws = ops.quantize_weight_128x128(weights(N, K, seed=seed).to(dev))
+    m.weight.data, m.weight_scale.data = wq, ws
+    m.bias.data = make_bias(N, seed=seed + 1).to(dev)
+    return m
+
+
+@pytest.mark.parametrize("rows,chunk,pinned", [(3000, 1024, True), (1000, 4096, True), (777, 256, False)])
+def test_ffn_streamed_equals_whole_batch(cuda_device, rows, chunk, pinned):
+    from ltx_kernels.blockwise import BlockwiseFP8FeedForward, TokenStreamer, ops
+    D, H = 512, 1024
+    ff = BlockwiseFP8FeedForward.from_linears(_linear(D, H, cuda_device, 1), _linear(H, D, cuda_device, 2))
+    x = activations(rows, D, seed=rows)
+    # the GEMM plans at the chunk and batch row counts agree here: results are bit-identical
+    for m in {rows, chunk, rows % chunk or chunk}:
+        assert ops.gemm_plan(m, H, D, cuda_device)["splits"] == 1
+        assert ops.gemm_plan(m, D, H, cuda_device)["splits"] == 1
+    with torch.inference_mode():
+        ref = ff(x.to(cuda_device)[None])[0].cpu()
+        xh = x.pin_memory() if pinned else x.clone()
+        out = torch.empty(rows, D, dtype=torch.bfloat16)
+        out = out.pin_memory() if pinned else out
+        st = TokenStreamer(ff, D, chunk, cuda_device)
+        for _ in range(2):  # reused slots and events across calls
+            out.fill_(0)
+            st(xh, out)
+            torch.cuda.current_stream().synchronize()
+            assert torch.equal(out, ref)
+
+
+def test_lora_linear_streamed(cuda_device):
+    from ltx_kernels.blockwise import stream_tokens
+    K, N, rows = 1024, 768, 1500
+    lin = _linear(K, N, cuda_device, 5, lora_rank=32)
+    x = activations(rows, K, seed=9)
+    with torch.inference_mode():
+        ref = lin(x.to(cuda_device)[None])[0].cpu()
+        out = stream_tokens(lin, x.pin_memory(), torch.empty(rows, N, dtype=torch.bfloat16).pin_memory(),
+                            chunk_tokens=512)
+        torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
+def test_stream_ordering_against_caller_stream(cuda_device):
+    """Work queued on the caller's stream before the call is visible to the layer, and
+    events recorded after the call cover the last copy."""
+    from ltx_kernels.blockwise import stream_tokens
+    K, N, rows = 512, 512, 2048
+    lin = _linear(K, N, cuda_device, 11)
+    x = activations(rows, K, seed=3)
+    xh = x.pin_memory()
+    out = torch.empty(rows, N, dtype=torch.bfloat16).pin_memory()
+    with torch.inference_mode():
+        ref = lin(x.to(cuda_device)[None])[0].cpu()
+        e1 = torch.cuda.Event()
+        torch.cuda._sleep(2_000_000)  # caller-stream work ahead of the call
+        stream_tokens(lin, xh, out, chunk_tokens=512)
+        e1.record()
+        e1.synchronize()
+    assert torch.equal(out, ref)
+
+
+def test_stream_rejects_bad_buffers(cuda_device):
+    from ltx_kernels.blockwise import TokenStreamer
+    st = TokenStreamer(lambda t: t, 256, 128, cuda_device)
+    with pytest.raises(RuntimeError):
+        st(torch.zeros(10, 256, dtype=torch.bfloat16, device=cuda_device), torch.zeros(10, 256, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError):
+        st(torch.zeros(10, 128, dtype=torch.bfloat16), torch.zeros(10, 256, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError):
+        st(torch.zeros(10, 256, dtype=torch.bfloat16), torch.zeros(9, 256, dtype=torch.bfloat16))
