@@ -9,7 +9,7 @@
 //
 // Design (one CTA per SM, persistent over 128 x 256 output tiles):
 //   warp 0      TMA producer: one 128-wide K block of A (16 KB) and W (32 KB)
-//               per pipeline stage, 4 stages, 128 B swizzle.
+//               per pipeline stage, 3 stages, 128 B swizzle.
 //   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (M128 N256 K32) per K
 //               block into one of two 256-column TMEM buffers, then
 //               tcgen05.commit to release the smem stage and hand the TMEM
@@ -20,8 +20,14 @@
 //               sfa[m,kb] * sfb[nb,kb] (the same promotion the reference does
 //               after every 128-K block, gemm.cu:185-199).  The two TMEM buffers
 //               let the tensor core run one K block ahead of the promotion.
-//               After the last block: + bias, optional GELU-tanh, optional
-//               1x128 requantisation to e4m3 for the next layer, stores.
+//               After the last block: y = bf16(acc + bias), optionally
+//               GELU-tanh (rounded to bf16), into a 64 KB shared staging tile,
+//               plus the abs-max of the thread's 1x128 group when the output is
+//               requantised, then straight on to the next tile.
+//   warps 2-3   drain the staging tile with TMA stores: the bf16 tile, and/or
+//               its 1x128 requantisation to e4m3 for the next layer (codes
+//               written over the consumed bf16, then stored by TMA), so that
+//               work overlaps the next tile's K loop.
 //   LoRA        alpha * (x A^T) B^T is folded in as extra K blocks of bf16 MMAs
 //               (kind::f16) over [x A^T | B], promoted with scale alpha.
 #pragma once
@@ -33,14 +39,17 @@ namespace ltxfp8 {
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 128;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr uint32_t kABytes = kBM * kBK;               // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK;               // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;   // 48 KB
+constexpr uint32_t kStagingBytes = kBM * kBN * 2;     // 64 KB: bf16 [128, 256] epilogue tile
 constexpr int kGemmThreads = 384;
 constexpr uint32_t kTmemCols = 512;                   // 2 x 256 fp32 accumulator columns
 constexpr int kLoraChunk = 64;                        // bf16 K elements per LoRA block (128 B rows)
-constexpr uint32_t kGemmSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kStagingAmaxBytes = 2 * kBM * 4;  // abs-max per (128-column half, row)
+constexpr uint32_t kGemmSmemBytes =
+    kStages * kStageBytes + kStagingBytes + kStagingAmaxBytes + 1024 /*align*/ + 256 /*barriers*/;
 
 // Register split between the producer/MMA warpgroup and the two epilogue
 // warpgroups; the launch must provide kGemmThreads * kGemmLaunchRegs.
@@ -62,6 +71,8 @@ enum GemmStatus : unsigned int {
   kStMmaFull = 0x47010003u,
   kStEpiTmemFull = 0x47010004u,
   kStDrain = 0x47010005u,
+  kStStagingFull = 0x47010006u,
+  kStStagingEmpty = 0x47010007u,
 };
 
 struct GemmParams {
@@ -120,6 +131,18 @@ __device__ __forceinline__ GemmUnit gemm_unit(int u, const GemmParams& p) {
 
 constexpr int kScalePrefetch = 4;
 
+// Epilogue staging tile, bf16 [128, 256], as four 16 KB column blocks of 64
+// columns (block b: columns 64b .. 64b+63), each laid out as TMA's 128 B swizzle
+// expects for a [rows, 64] bf16 box: row r at r * 128, its 16 B chunk c (8
+// columns) at position c ^ (r & 7).  32 lanes touching one chunk of 32
+// consecutive rows then spread over all banks, and any 32-row slice of a block is
+// itself a valid TMA box.  `chunk` counts 8-column chunks across the tile (0..31).
+constexpr uint32_t kStagingBlockBytes = kBM * 128;  // 16 KB
+__device__ __forceinline__ uint32_t gemm_staging_off(int r, int chunk) {
+  return static_cast<uint32_t>(chunk >> 3) * kStagingBlockBytes + static_cast<uint32_t>(r) * 128u +
+         static_cast<uint32_t>(((chunk & 7) ^ (r & 7)) * 16);
+}
+
 // Fold one K block's raw partial sums (TMEM buffer `it & 1`) into the fp32
 // accumulators of this thread's row: acc += scale * partial, 128 columns as 64
 // packed f32x2 FMAs.  Releases the TMEM buffer as soon as it has been read.
@@ -158,15 +181,20 @@ template <bool kGelu, bool kRequant>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     fp8_blockwise_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                               const __grid_constant__ CUtensorMap tmLX, const __grid_constant__ CUtensorMap tmLB,
+                              const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmQ,
                               const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* staging = smem + kStages * kStageBytes;
+  float* stg_amax = reinterpret_cast<float*>(staging + kStagingBytes);  // [2 halves][128 rows]
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kStagingBytes + kStagingAmaxBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;   // [2]
   uint64_t* tempty = tfull + 2;        // [2]
-  uint64_t* drain = tempty + 2;        // [1]
+  uint64_t* stg_full = tempty + 2;     // [1] promotion warps -> store warps
+  uint64_t* stg_empty = stg_full + 1;  // [1] store warps -> promotion warps
+  uint64_t* drain = stg_empty + 1;     // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
@@ -181,6 +209,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);  // one arrival per epilogue warp
     }
+    mbar_init(stg_full, 8);      // one arrival per promotion warp
+    mbar_init(stg_empty, 2);     // one arrival per store warp
     mbar_init(drain, 1);
     fence_mbarrier_init();
   }
@@ -190,6 +220,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (p.num_lora > 0) {
       tma_prefetch_desc(&tmLX);
       tma_prefetch_desc(&tmLB);
+    }
+    if (p.k_splits == 1) {
+      if (p.flags & kGemmWriteD) tma_prefetch_desc(&tmD);
+      if (kRequant) tma_prefetch_desc(&tmQ);
     }
   }
   if (warp == 1) {
@@ -277,6 +311,98 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Every MMA this thread issued has completed once `drain` flips.
       tc_commit(drain);
       mbar_wait(drain, 0u, kStDrain);
+    } else if (warp >= 2 && p.k_splits == 1) {
+      // ------------------------------------------------------------ staging -> global (warps 2, 3)
+      // (Whole warps 2 and 3 only: lanes 1-31 of warps 0 and 1 must not enter,
+      // their lane 0 never joins the warp-wide votes below.)  Warp pw owns the
+      // 32-row slices pw*32 and 64 + pw*32 of the tile: its passes and stores need
+      // no synchronisation with the other store warp.  Lane 0 issues the TMA stores.
+      const int pw = warp - 2;
+      const bool write_d = (p.flags & kGemmWriteD) != 0;
+      uint32_t tcount = 0;
+      for (int u = blockIdx.x; u < p.total_tiles; u += gridDim.x, ++tcount) {
+        int mt, nt;
+        gemm_tile_coords(u, p, mt, nt);
+        const int m0 = mt * kBM, n0 = nt * kBN;
+        if (!__all_sync(0xffffffffu, mbar_wait(stg_full, tcount & 1u, kStStagingFull))) break;
+        if constexpr (kRequant) {
+          // 1x128 requantisation of the staged bf16 values (the reference
+          // quantises the bf16 GEMM / GELU output).  One lane per group: step j
+          // covers 32 consecutive rows of one 128-column half.  If D is wanted the
+          // bf16 slice goes out first; the codes are then written over the slice's
+          // first column block and go out as one TMA box.
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            const int g = j & 1;
+            const int rb = (j >> 1) * 64 + pw * 32;
+            const int r = rb + lane;
+            const int col0 = n0 + g * 128;
+            if (col0 >= p.N) continue;  // warp-uniform: N % 128 == 0
+            const bool slice_ok = m0 + rb < p.M;
+            if (write_d) {
+              if (lane == 0 && slice_ok) {
+                tma_store_2d(&tmD, staging + (2 * g) * kStagingBlockBytes + rb * 128, col0, m0 + rb);
+                tma_store_2d(&tmD, staging + (2 * g + 1) * kStagingBlockBytes + rb * 128, col0 + 64, m0 + rb);
+                tma_store_commit();
+                tma_store_wait_read();  // the codes below overwrite the slice
+              }
+              __syncwarp();
+            }
+            const float s = __fmul_rn(__frcp_rn(stg_amax[g * kBM + r]), 448.0f);
+            const bool in_range = isfinite(s);  // then no product exceeds 448: plain hardware conversion
+            uint8_t* qrow = staging + (2 * g) * kStagingBlockBytes + r * 128;
+#pragma unroll 1
+            for (int k = 0; k < 8; ++k) {  // 16 codes from bf16 chunks 2k, 2k+1
+              uint32_t w4[4];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 v = *reinterpret_cast<const uint4*>(staging + gemm_staging_off(r, g * 16 + 2 * k + h));
+                float f[8];
+                bf16x8_to_f32(v, f);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  const float v0 = __fmul_rn(f[4 * i], s), v1 = __fmul_rn(f[4 * i + 1], s);
+                  const float v2 = __fmul_rn(f[4 * i + 2], s), v3 = __fmul_rn(f[4 * i + 3], s);
+                  const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+                  const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
+                  w4[2 * h + i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+                }
+              }
+              // Code chunk k replaces bf16 chunk k of the block, already read (k <= 2k).
+              *reinterpret_cast<uint4*>(qrow + ((k ^ (r & 7)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            if (m0 + r < p.M) p.s_out[static_cast<int64_t>(col0 / 128) * p.s_out_ld + m0 + r] = __frcp_rn(s);
+            __syncwarp();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && slice_ok) {
+              tma_store_2d(&tmQ, staging + (2 * g) * kStagingBlockBytes + rb * 128, col0, m0 + rb);
+              tma_store_commit();
+            }
+          }
+        } else {
+          // bf16 D (GELU already applied by the promotion warps): the tile goes out
+          // as staged (the promotion warps fenced it for the async proxy).
+          if (lane == 0) {
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              const int rb = h * 64 + pw * 32;
+              if (m0 + rb >= p.M) continue;
+#pragma unroll 1
+              for (int b4 = 0; b4 < 4; ++b4)
+                if (n0 + b4 * 64 < p.N)
+                  tma_store_2d(&tmD, staging + b4 * kStagingBlockBytes + rb * 128, n0 + b4 * 64, m0 + rb);
+            }
+            tma_store_commit();
+          }
+        }
+        // The staging tile may be overwritten once the stores have read it.
+        if (lane == 0) tma_store_wait_read();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stg_empty);
+      }
+      if (lane == 0) tma_store_wait_all();
+      __syncwarp();
     }
   } else {
     setmaxnreg_inc<kRegsEpi>();
@@ -284,6 +410,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int sp = warp & 3;          // TMEM sub-partition: rows 32*sp .. 32*sp+31
     const int half = (warp - 4) >> 2; // which 128-column half of the 256-wide tile
     uint32_t it = 0;
+    uint32_t tcount = 0;              // staged tiles so far (staging barrier phases)
     bool ok = true;
     const int total_units = p.total_tiles * p.k_splits;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
@@ -325,71 +452,59 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (!ok) break;
-      if (!(row_ok && col_ok)) continue;
       if (p.k_splits > 1) {
         // Split-K unit: the raw fp32 partial (no bias) for the reduction kernel.
+        if (!(row_ok && col_ok)) continue;
         float4* dst = reinterpret_cast<float4*>(p.ws + (static_cast<int64_t>(u) * kBM + sp * 32 + lane) * kBN +
                                                 half * 128);
 #pragma unroll
         for (int c = 0; c < 32; ++c) dst[c] = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
         continue;
       }
-      float* accf = reinterpret_cast<float*>(acc);
-
-      // ------------------------------------------------ bias (+ GELU) in fp32, bf16 rounding
-      const bool has_bias = (p.flags & kGemmBias) != 0;
+      // bf16(acc + bias) into the staging tile once the store warps have drained
+      // the previous one.  Every promotion warp arrives once per tile, in range or not.
+      if (!__all_sync(0xffffffffu, mbar_wait(stg_empty, (tcount & 1u) ^ 1u, kStStagingEmpty))) {
+        ok = false;
+        break;
+      }
+      const bool has_bias = (p.flags & kGemmBias) != 0 && col_ok;
       const float4* bias4 = reinterpret_cast<const float4*>(p.bias + col0);
+      const int r_local = sp * 32 + lane;
+      float gmax = 0.0f;  // abs-max of this thread's 1x128 group (requant)
 #pragma unroll
-      for (int c = 0; c < 128; c += 4) {
-        float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (has_bias) bv = __ldg(bias4 + c / 4);
-        accf[c] += bv.x;
-        accf[c + 1] += bv.y;
-        accf[c + 2] += bv.z;
-        accf[c + 3] += bv.w;
-      }
-      if constexpr (kGelu || kRequant) {
-        // The reference materialises bf16(acc + bias), applies GELU on that bf16
-        // tensor (result rounded to bf16) and quantises those bf16 values.
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          float y = bf16_round(accf[c]);
-          if constexpr (kGelu) y = bf16_round(gelu_tanh_f32(y));
-          accf[c] = y;
+      for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 columns
+        float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+        if (has_bias) {
+          b0 = __ldg(bias4 + 2 * c);
+          b1 = __ldg(bias4 + 2 * c + 1);
         }
-      }
-      const int64_t out_off = static_cast<int64_t>(row) * p.N + col0;
-      if (p.flags & kGemmWriteD) {
-        uint4* dst = reinterpret_cast<uint4*>(p.d + out_off);
-#pragma unroll
-        for (int c = 0; c < 128; c += 8) {
-          dst[c / 8] = make_uint4(pack_bf16x2(accf[c], accf[c + 1]), pack_bf16x2(accf[c + 2], accf[c + 3]),
-                                  pack_bf16x2(accf[c + 4], accf[c + 5]), pack_bf16x2(accf[c + 6], accf[c + 7]));
-        }
-      }
-      if constexpr (kRequant) {
-        // One thread owns the whole 1x128 group of its row: no cross-thread reduction.
-        float amax = 0.0f;
-#pragma unroll
-        for (int c = 0; c < 128; ++c) amax = fmax_nan(amax, fabsf(accf[c]));
-        const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
-        const bool in_range = isfinite(s);  // then no product exceeds 448: plain hardware conversion
-        uint4* qdst = reinterpret_cast<uint4*>(p.q_out + out_off);
-#pragma unroll
-        for (int c = 0; c < 128; c += 16) {
-          uint32_t w[4];
+        const float2 a0 = acc[4 * c], a1 = acc[4 * c + 1], a2 = acc[4 * c + 2], a3 = acc[4 * c + 3];
+        uint32_t w4[4] = {pack_bf16x2(a0.x + b0.x, a0.y + b0.y), pack_bf16x2(a1.x + b0.z, a1.y + b0.w),
+                          pack_bf16x2(a2.x + b1.x, a2.y + b1.y), pack_bf16x2(a3.x + b1.z, a3.y + b1.w)};
+        if constexpr (kGelu) {
+          // The reference applies GELU to the bf16 tensor bf16(acc + bias) and
+          // rounds the result to bf16.
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float v0 = __fmul_rn(accf[c + 4 * i], s), v1 = __fmul_rn(accf[c + 4 * i + 1], s);
-            const float v2 = __fmul_rn(accf[c + 4 * i + 2], s), v3 = __fmul_rn(accf[c + 4 * i + 3], s);
-            const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
-            const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
-            w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+            const float2 y =
+                gelu_tanh_f32x2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)));
+            w4[i] = pack_bf16x2(y.x, y.y);
           }
-          qdst[c / 16] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        p.s_out[static_cast<int64_t>(nb) * p.s_out_ld + row] = __frcp_rn(s);
+        if constexpr (kRequant) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            gmax = fmax_nan(gmax, fmax_nan(fabsf(__uint_as_float(w4[i] << 16)),
+                                           fabsf(__uint_as_float(w4[i] & 0xFFFF0000u))));
+        }
+        *reinterpret_cast<uint4*>(staging + gemm_staging_off(r_local, half * 16 + c)) =
+            make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
+      if constexpr (kRequant) stg_amax[half * kBM + r_local] = gmax;
+      fence_proxy_async_smem();  // the store warps may hand these bytes straight to TMA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(stg_full);
+      ++tcount;
     }
   }
 

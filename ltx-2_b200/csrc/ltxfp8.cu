@@ -141,12 +141,13 @@ int gemm_prepare(DeviceInfo* d) {
 
 template <bool kGelu, bool kRequant>
 int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
-                const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
+                const CUtensorMap& lb, const CUtensorMap& md, const CUtensorMap& mq, const GemmParams& p,
+                cudaStream_t stream) {
   int rc = gemm_prepare<kGelu, kRequant>(d);
   if (rc) return rc;
   const int units = p.total_tiles * p.k_splits;
   const int grid = units < d->sms ? units : d->sms;
-  fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, p);
+  fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, md, mq, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return LTXFP8_OK;
@@ -248,8 +249,9 @@ int splitk_reduce_launch(const DeviceInfo* d, const GemmParams& p, cudaStream_t 
 
 template <bool kGelu, bool kRequant>
 int gemm_launch_full(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
-                     const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
-  int rc = gemm_launch<kGelu, kRequant>(d, a, b, lx, lb, p, stream);
+                     const CUtensorMap& lb, const CUtensorMap& md, const CUtensorMap& mq, const GemmParams& p,
+                     cudaStream_t stream) {
+  int rc = gemm_launch<kGelu, kRequant>(d, a, b, lx, lb, md, mq, p, stream);
   if (rc || p.k_splits == 1) return rc;
   return splitk_reduce_launch<kGelu, kRequant>(d, p, stream);
 }
@@ -831,10 +833,23 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
     if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, p, stream);
     return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, p, stream);
   }
-  if (gelu && requant) return gemm_launch_full<true, true>(d, ma, mb, mlx, mlb, p, stream);
-  if (gelu) return gemm_launch_full<true, false>(d, ma, mb, mlx, mlb, p, stream);
-  if (requant) return gemm_launch_full<false, true>(d, ma, mb, mlx, mlb, p, stream);
-  return gemm_launch_full<false, false>(d, ma, mb, mlx, mlb, p, stream);
+  // Output maps for the staged epilogue's TMA stores: bf16 D in [32, 64] boxes,
+  // e4m3 codes in [32, 128] boxes, 128 B swizzle (the staging tile's layout).
+  CUtensorMap md = ma, mq = ma;
+  if (!split) {
+    if (write_d) {
+      rc = make_map_2d(&md, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.d, N, rows, N * 2, 64, 32);
+      if (rc) return rc;
+    }
+    if (e.requant_q) {
+      rc = make_map_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.q_out, N, rows, N, 128, 32);
+      if (rc) return rc;
+    }
+  }
+  if (gelu && requant) return gemm_launch_full<true, true>(d, ma, mb, mlx, mlb, md, mq, p, stream);
+  if (gelu) return gemm_launch_full<true, false>(d, ma, mb, mlx, mlb, md, mq, p, stream);
+  if (requant) return gemm_launch_full<false, true>(d, ma, mb, mlx, mlb, md, mq, p, stream);
+  return gemm_launch_full<false, false>(d, ma, mb, mlx, mlb, md, mq, p, stream);
 }
 
 int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,

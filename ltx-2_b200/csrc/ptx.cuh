@@ -99,6 +99,22 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
 }
 
 // ---------------------------------------------------------------- tcgen05
+// Tiled TMA store, shared -> global, tracked by the issuing thread's bulk groups.
+// Elements of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory sources of this thread's committed stores have been read.
+__device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's committed stores are complete.
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy
+// (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
                "r"(ncols)
@@ -348,17 +364,38 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+
 // GELU with the tanh approximation, the function torch evaluates for
 // F.gelu(x, approximate="tanh"): 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3).
 // Evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)), i.e.
-// gelu = x / (1 + exp(-2u)), with the fast exp and divide intrinsics (relative
-// error ~1e-6, far below the bf16 rounding the result goes through).  Unlike
-// 1 + tanh(u) the identity has no cancellation for negative x.
+// gelu = x / (1 + 2^a) with the exponent folded into one base-2 argument
+// a = x (c1 + c3 x^2), c1 = -2 sqrt(2/pi) log2(e), c3 = 0.044715 c1, and the
+// hardware ex2 / reciprocal approximations (relative error ~1e-7, far below the
+// bf16 rounding the result goes through).  Unlike 1 + tanh(u) the identity has
+// no cancellation for negative x.  The scalar and the packed f32x2 forms perform
+// the same roundings, so every kernel rounds GELU identically.
+__device__ __forceinline__ float ex2_approx(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+constexpr float kGeluC1 = -2.0f * 0.7978845608028654f * 1.4426950408889634f;
+constexpr float kGeluC3 = kGeluC1 * 0.044715f;
 __device__ __forceinline__ float gelu_tanh_f32(float x) {
-  const float kBeta = 0.7978845608028654f;
-  const float kKappa = 0.044715f;
-  const float u = kBeta * fmaf(kKappa * x * x, x, x);
-  return __fdividef(x, 1.0f + __expf(-2.0f * u));
+  const float a = __fmul_rn(__fmaf_rn(__fmul_rn(x, x), kGeluC3, kGeluC1), x);
+  return __fmul_rn(x, rcp_approx(__fadd_rn(ex2_approx(a), 1.0f)));
+}
+__device__ __forceinline__ float2 gelu_tanh_f32x2(float2 x) {
+  const float kC1 = kGeluC1, kC3 = kGeluC3;
+  const float2 x2 = __fmul2_rn(x, x);
+  const float2 a = __fmul2_rn(__ffma2_rn(x2, make_float2(kC3, kC3), make_float2(kC1, kC1)), x);
+  const float2 d = __fadd2_rn(make_float2(ex2_approx(a.x), ex2_approx(a.y)), make_float2(1.0f, 1.0f));
+  return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
 }
 
 }  // namespace ltxfp8
