@@ -790,7 +790,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=0, help="tokens per GPU (default: the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-chunk", type=int, default=3072,
+    ap.add_argument("--e2e-chunk", type=int, default=2048,
                     help="ffn/linear/qkv_lora e2e: tokens per streamed chunk (0: whole batch, copies not overlapped)")
     ap.add_argument("--no-graph", action="store_true", help="dit_step: launch every GEMM from Python instead of "
                                                              "replaying a captured CUDA graph")

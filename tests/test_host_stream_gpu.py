@@ -31,8 +31,12 @@ def test_ffn_streamed_equals_whole_batch(cuda_device, rows, chunk, pinned):
     D, H = 512, 1024
     ff = BlockwiseFP8FeedForward.from_linears(_linear(D, H, cuda_device, 1), _linear(H, D, cuda_device, 2))
     x = activations(rows, D, seed=rows)
+    st = TokenStreamer(ff, D, chunk, cuda_device)
+    b = st.bounds(rows)
+    sizes = [b[i + 1] - b[i] for i in range(len(b) - 1)]
+    assert b[0] == 0 and b[-1] == rows and min(sizes) > 0 and max(sizes) <= chunk
     # the GEMM plans at the chunk and batch row counts agree here: results are bit-identical
-    for m in {rows, chunk, rows % chunk or chunk}:
+    for m in set(sizes) | {rows}:
         assert ops.gemm_plan(m, H, D, cuda_device)["splits"] == 1
         assert ops.gemm_plan(m, D, H, cuda_device)["splits"] == 1
     with torch.inference_mode():
@@ -40,7 +44,6 @@ def test_ffn_streamed_equals_whole_batch(cuda_device, rows, chunk, pinned):
         xh = x.pin_memory() if pinned else x.clone()
         out = torch.empty(rows, D, dtype=torch.bfloat16)
         out = out.pin_memory() if pinned else out
-        st = TokenStreamer(ff, D, chunk, cuda_device)
         for _ in range(2):  # reused slots and events across calls
             out.fill_(0)
             st(xh, out)
