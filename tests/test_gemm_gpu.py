@@ -391,3 +391,37 @@ def test_tail_wave_split(cuda_device, M, N, K):
     assert torch.equal(dl[:r0], dl1[:r0])
     diff = (dl.float() - dl1.float()).abs().max().item()
     assert diff <= 0.02 * dl1.float().abs().max().item()
+
+
+# --------------------------------------------------------------------------- staged epilogue
+@pytest.mark.parametrize("M,N,K", [(37, 384, 512), (130, 640, 256), (1, 128, 128), (300, 1152, 1024)])
+@pytest.mark.parametrize("gelu,requant,write_d", [(False, False, True), (True, False, True), (False, True, True),
+                                                  (False, True, False), (True, True, True), (True, True, False)])
+def test_staged_epilogue_combinations(cuda_device, M, N, K, gelu, requant, write_d):
+    """Every epilogue combination through the staging tile and the TMA stores, at ragged
+    M (rows beyond M inside a tile) and N with an empty 128-column half tile: values
+    against the oracle, codes bit-exact against quantising the bf16 result, and no row
+    beyond M written (the output is a view into a larger buffer holding a sentinel)."""
+    from ltx_kernels.blockwise import ops
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=M * 7 + N)
+    ref = _oracle(aq, asc, wq, wsc, b)
+    if gelu:
+        ref = O.bf16_to_f32(O.gelu_tanh_bf16(O.f32_to_bf16(ref)))
+    pad = 130
+    big = torch.full((M + pad, N), -7.25, dtype=torch.bfloat16, device=cuda_device)
+    res = ops.gemm(aq, asc, wq, wsc, b, out=big[:M], gelu=gelu, requant=requant, write_d=write_d, split_k=False)
+    torch.cuda.synchronize()
+    assert (big[M:] == -7.25).all()
+    if requant:
+        d, q, s = res
+        # the bf16 values the codes quantise: this call's D, or the same GEMM with D written
+        dd = d if write_d else ops.gemm(aq, asc, wq, wsc, b, gelu=gelu, split_k=False)
+        oq, os_ = O.quant_act_1x128(bits(dd))
+        assert O.codes_equal(bits(q), oq).all()
+        assert O.scales_equal(scales_mn(s, M), os_[:, :M]).all()
+        if not write_d:
+            assert d is None and (big == -7.25).all()
+            return
+    else:
+        d = res
+    _check(d, ref)
