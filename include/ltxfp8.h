@@ -239,8 +239,15 @@ typedef struct ltxfp8_gemm_plan_info {
   int64_t split_row0;     /* rows [0, split_row0) unsplit, [split_row0, M) split; M: no split */
 } ltxfp8_gemm_plan_info;
 
-/* Fills *info for an M x N x K GEMM (no reference counterpart). */
+/* Fills *info for an M x N x K GEMM on the current device (no reference counterpart). */
 int ltxfp8_gemm_plan(int64_t M, int64_t N, int64_t K, ltxfp8_gemm_plan_info* info);
+
+/* The same plan for a GPU with `sms` streaming multiprocessors; a host computation
+   only (no CUDA call), for planning and tests without a device. */
+int ltxfp8_gemm_plan_for_sms(int64_t M, int64_t N, int64_t K, int sms, ltxfp8_gemm_plan_info* info);
+
+/* Size of the static split-K array of ltxfp8_gemm_static_scratch. */
+#define LTXFP8_STATIC_SCRATCH_BYTES (32ull << 20)
 
 /*
  * ltxfp8_gemm for callers that cannot allocate device memory per call: a host

@@ -28,7 +28,7 @@ using namespace ltxfp8;
 // covers the split-K plan of every shape on a 148-SM device: each split unit
 // keeps a 128 x 256 fp32 block (128 KiB) and the split units of a launch fit in
 // one wave (at most sms = 148 units, 18.5 MiB).
-constexpr size_t kStaticScratchBytes = 32ull << 20;
+constexpr size_t kStaticScratchBytes = LTXFP8_STATIC_SCRATCH_BYTES;
 static __device__ __align__(256) float g_gemm_static_scratch[kStaticScratchBytes / sizeof(float)];
 
 namespace {
@@ -165,10 +165,10 @@ struct SplitPlan {
   int splits, kb_per_split;
 };
 
-SplitPlan splitk_plan(const DeviceInfo* d, int64_t total_tiles, int64_t num_kb) {
+SplitPlan splitk_plan(int sms, int64_t total_tiles, int64_t num_kb) {
   SplitPlan pl{1, static_cast<int>(num_kb)};
-  if (num_kb < 4 || total_tiles * 2 > d->sms) return pl;
-  int64_t max_s = d->sms / total_tiles;
+  if (num_kb < 4 || total_tiles * 2 > sms) return pl;
+  int64_t max_s = sms / total_tiles;
   if (max_s > num_kb / 2) max_s = num_kb / 2;
   if (max_s > 16) max_s = 16;
   double best = static_cast<double>(num_kb);
@@ -206,21 +206,21 @@ struct GemmPlan {
   SplitPlan split;      // split.splits == 1: no split launch
 };
 
-GemmPlan gemm_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K) {
+GemmPlan gemm_plan(int sms, int64_t M, int64_t N, int64_t K) {
   const int64_t m_tiles = (M + kBM - 1) / kBM, n_tiles = (N + kBN - 1) / kBN;
   const int64_t tiles = m_tiles * n_tiles, num_kb = K / kBK;
   GemmPlan g{M, 0, SplitPlan{1, static_cast<int>(num_kb)}};
-  if (tiles * 2 <= d->sms) {
-    const SplitPlan sp = splitk_plan(d, tiles, num_kb);
+  if (tiles * 2 <= sms) {
+    const SplitPlan sp = splitk_plan(sms, tiles, num_kb);
     if (sp.splits > 1) g = GemmPlan{0, tiles, sp};
     return g;
   }
-  const int64_t rem = tiles % d->sms;
-  if (num_kb < kTailSplitMinKb || rem == 0 || rem * 2 > d->sms) return g;
+  const int64_t rem = tiles % sms;
+  if (num_kb < kTailSplitMinKb || rem == 0 || rem * 2 > sms) return g;
   const int64_t tail_m_tiles = (rem + n_tiles - 1) / n_tiles;
   const int64_t tail_tiles = tail_m_tiles * n_tiles;
-  if (tail_m_tiles >= m_tiles || tail_tiles * 2 > d->sms) return g;
-  const SplitPlan sp = splitk_plan(d, tail_tiles, num_kb);
+  if (tail_m_tiles >= m_tiles || tail_tiles * 2 > sms) return g;
+  const SplitPlan sp = splitk_plan(sms, tail_tiles, num_kb);
   if (sp.splits > 1) g = GemmPlan{(m_tiles - tail_m_tiles) * kBM, tail_tiles, sp};
   return g;
 }
@@ -892,7 +892,7 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   auto s = static_cast<cudaStream_t>(stream);
   const bool use_pair = g_gemm_variant.load() == 2;
   if (use_pair) return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, true, s);
-  const GemmPlan g = gemm_plan(d, M, N, K);
+  const GemmPlan g = gemm_plan(d->sms, M, N, K);
   const size_t need = splitk_bytes(g);
   if (need == 0 || !e.workspace || need > e.workspace_bytes)
     return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, false, s);
@@ -912,7 +912,25 @@ int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) 
   DeviceInfo* d;
   int rc = device_info(&d);
   if (rc) return rc;
-  *bytes = splitk_bytes(gemm_plan(d, M, N, K));
+  *bytes = splitk_bytes(gemm_plan(d->sms, M, N, K));
+  return LTXFP8_OK;
+}
+
+int ltxfp8_gemm_plan_for_sms(int64_t M, int64_t N, int64_t K, int sms, ltxfp8_gemm_plan_info* info) {
+  if (!info) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm_plan: null pointer");
+  memset(info, 0, sizeof(*info));
+  if (M < 1 || N < 128 || K < 128 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gemm_plan: need M >= 1 and N, K positive multiples of 128");
+  if (sms < 1) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm_plan: sms must be positive");
+  info->launches = 1;
+  info->splits = 1;
+  info->split_row0 = M;
+  const GemmPlan g = gemm_plan(sms, M, N, K);
+  if (g.split.splits < 2) return LTXFP8_OK;
+  info->workspace_bytes = splitk_bytes(g);
+  info->launches = gemm_plan_launches(g);
+  info->splits = g.split.splits;
+  info->split_row0 = g.split_row0;
   return LTXFP8_OK;
 }
 
@@ -928,13 +946,7 @@ int ltxfp8_gemm_plan(int64_t M, int64_t N, int64_t K, ltxfp8_gemm_plan_info* inf
   DeviceInfo* d;
   int rc = device_info(&d);
   if (rc) return rc;
-  const GemmPlan g = gemm_plan(d, M, N, K);
-  if (g.split.splits < 2) return LTXFP8_OK;
-  info->workspace_bytes = splitk_bytes(g);
-  info->launches = gemm_plan_launches(g);
-  info->splits = g.split.splits;
-  info->split_row0 = g.split_row0;
-  return LTXFP8_OK;
+  return ltxfp8_gemm_plan_for_sms(M, N, K, d->sms, info);
 }
 
 int ltxfp8_gemm_static_scratch(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,

@@ -78,6 +78,7 @@ SIGNATURES = {
     "ltxfp8_gemm_set_variant": (_i32, [_i32]),
     "ltxfp8_gemm_workspace_bytes": (_i32, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
     "ltxfp8_gemm_plan": (_i32, [_i64, _i64, _i64, _vp]),
+    "ltxfp8_gemm_plan_for_sms": (_i32, [_i64, _i64, _i64, _i32, _vp]),
     "ltxfp8_adanorm_quantize": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i32,
                                         _vp]),
     "ltxfp8_rms_fma": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),
