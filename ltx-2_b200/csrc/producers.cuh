@@ -143,7 +143,7 @@ __device__ __forceinline__ float sumsq_chunk(float acc, const uint4& v) {
 
 // x bf16 [B*S, H]; scale/shift element (b, s, h) at p[b * bstride + s * sstride + h].
 template <int kChunks, int kMode>
-__global__ void __launch_bounds__(kProdWarps * 32, 4) adanorm_quant_kernel(
+__global__ void __launch_bounds__(kProdWarps * 32, 8) adanorm_quant_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t M, int64_t S, int H, const __nv_bfloat16* __restrict__ scale,
     int64_t scale_bs, int64_t scale_ss, const __nv_bfloat16* __restrict__ shift, int64_t shift_bs, int64_t shift_ss,
     ProducerOut o) {
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kProdWarps * 32, 4) adanorm_quant_kernel(
 // (o.q) or rounded to bf16 (o.out).  The second pass reads back the updated x
 // (this thread's own stores, through the coherent path).
 template <int kChunks, int kMode, bool kQuant>
-__global__ void __launch_bounds__(kProdWarps * 32, 4) rms_fma_kernel(__nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(kProdWarps * 32, 8) rms_fma_kernel(__nv_bfloat16* __restrict__ x,
                                                                    const __nv_bfloat16* __restrict__ y, int64_t M,
                                                                    int64_t S, int H,
                                                                    const __nv_bfloat16* __restrict__ z, int64_t z_bs,
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(kProdWarps * 32, 4) rms_fma_kernel(__nv_bfloat
 // x bf16 [M, H] viewed as [heads, H/heads]; gate_logits [M, heads] (bf16 or fp32);
 // o = x * 2 sigmoid(logit) in fp32, quantised or rounded to bf16.
 template <int kChunks, int kMode, bool kQuant, bool kGateF32>
-__global__ void __launch_bounds__(kProdWarps * 32) gated_attention_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(kProdWarps * 32, 8) gated_attention_kernel(const __nv_bfloat16* __restrict__ x,
                                                                         const void* __restrict__ gate_logits,
                                                                         int64_t M, int H, int heads, ProducerOut o) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l16 = lane & 15;
