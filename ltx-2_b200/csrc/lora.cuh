@@ -6,10 +6,11 @@
 // this kernel provides the x A^T half of a runtime alpha * B (A x) term whose
 // B half is folded into the FP8 GEMM as extra bf16 K blocks.
 //
-// One CTA per 128 rows: warp 0 streams 64-wide K chunks of x (16 KB) and A
-// (r x 128 B) through a TMA ring, warp 1 issues tcgen05.mma.kind::f16
-// (M128, N = r, K16) accumulating over all of K in TMEM, warps 4-7 drain the
-// r accumulator columns to bf16.
+// One CTA per 128 rows, two CTAs per SM (96 KB of ring each, so 24576 rows run
+// in one wave): warp 0 streams 64-wide K chunks of x (16 KB) and A (r x 128 B)
+// through a TMA ring, warp 1 issues tcgen05.mma.kind::f16 (M128, N = r, K16)
+// accumulating over all of K in TMEM, warps 4-7 drain the r accumulator columns
+// to bf16.
 #pragma once
 
 #include "ptx.cuh"
@@ -18,7 +19,7 @@ namespace ltxfp8 {
 
 constexpr int kLoraThreads = 256;
 constexpr uint32_t kLoraXBytes = 128 * 128;  // 128 rows x 64 bf16
-constexpr uint32_t kLoraSmemBudget = 192 * 1024;
+constexpr uint32_t kLoraSmemBudget = 96 * 1024;  // two CTAs per SM: one wave for 24576 rows
 
 enum LoraStatus : unsigned int {
   kStLoraProducer = 0x4C010001u,
@@ -36,7 +37,7 @@ struct LoraParams {
   __nv_bfloat16* ax;     // [M, r]
 };
 
-__global__ void __launch_bounds__(kLoraThreads, 1)
+__global__ void __launch_bounds__(kLoraThreads, 2)
     lora_a_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmA,
                   const LoraParams p) {
   extern __shared__ uint8_t smem_raw[];
