@@ -453,12 +453,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok) break;
       if (p.k_splits > 1) {
-        // Split-K unit: the raw fp32 partial (no bias) for the reduction kernel.
-        if (!(row_ok && col_ok)) continue;
-        float4* dst = reinterpret_cast<float4*>(p.ws + (static_cast<int64_t>(u) * kBM + sp * 32 + lane) * kBN +
-                                                half * 128);
+        // Split-K unit: the raw fp32 partial (no bias) for the reduction kernel,
+        // block u of the workspace, row-major 128 x 256.  A split launch runs one
+        // unit per CTA (units <= SMs), so the pipeline stages are idle here: each
+        // warp transposes its 32 rows x 128 columns through its own 16 KB of them
+        // and stores whole 512 B rows (lane = row would touch 32 lines per store).
+        if (!col_ok) continue;  // warp-uniform
+        uint8_t* tr = smem + static_cast<uint32_t>(warp - 4) * (32u * 512u);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) dst[c] = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
+        for (int c = 0; c < 32; ++c)
+          *reinterpret_cast<float4*>(tr + lane * 512 + ((c ^ (lane & 7)) * 16)) =
+              make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
+        __syncwarp();
+        float* wsu = p.ws + (static_cast<int64_t>(u) * kBM + sp * 32) * kBN + half * 128;
+#pragma unroll 4
+        for (int i = 0; i < 32; ++i) {
+          if (w.mt * kBM + sp * 32 + i >= p.M) break;  // warp-uniform
+          reinterpret_cast<float4*>(wsu + static_cast<int64_t>(i) * kBN)[lane] =
+              *reinterpret_cast<const float4*>(tr + i * 512 + ((lane ^ (i & 7)) * 16));
+        }
+        __syncwarp();
         continue;
       }
       // bf16(acc + bias) into the staging tile once the store warps have drained
