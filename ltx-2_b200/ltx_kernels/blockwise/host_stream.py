@@ -37,7 +37,15 @@ from typing import Callable, Optional
 
 import torch
 
-__all__ = ["stream_tokens", "TokenStreamer"]
+__all__ = ["chunk_bounds", "stream_tokens", "TokenStreamer"]
+
+
+def chunk_bounds(rows: int, chunk: int):
+    """Row boundaries [0, c, 2c, ..., rows] of a ``rows``-token call cut into chunks of
+    at most ``chunk`` tokens."""
+    if rows < 0 or chunk < 1:
+        raise ValueError("chunk_bounds: rows >= 0 and chunk >= 1 required")
+    return list(range(0, rows, chunk)) + [rows]
 
 
 class TokenStreamer:
@@ -66,7 +74,7 @@ class TokenStreamer:
 
     def bounds(self, rows: int):
         """Row boundaries of the chunks of a ``rows``-token call."""
-        return list(range(0, rows, self.chunk)) + [rows]
+        return chunk_bounds(rows, self.chunk)
 
     def __call__(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
         if x_host.is_cuda or out_host.is_cuda:
