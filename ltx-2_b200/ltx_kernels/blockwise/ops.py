@@ -29,9 +29,18 @@ def _stream(t: torch.Tensor) -> int:
 
 
 def _require_cuda(name: str, *ts: Optional[torch.Tensor]) -> None:
+    """CUDA tensors, all on one device (a kernel handed another GPU's pointer would read
+    memory its device may not map)."""
+    dev = None
     for t in ts:
-        if t is not None and not t.is_cuda:
+        if t is None:
+            continue
+        if not t.is_cuda:
             raise RuntimeError(f"{name}: ltx-2_b200 kernels need CUDA (sm_100) tensors, got {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{name}: all tensors must be on one device, got {dev} and {t.device}")
 
 
 class _DeviceGuard:
@@ -358,6 +367,9 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
         if bias.dtype != torch.float32 or bias.numel() != N:
             raise RuntimeError("gemm: bias must be fp32 [N] (the SM89 contract takes float*)")
         bias = bias.contiguous()
+    if out is not None and (out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or not out.is_contiguous()
+                            or out.device != a_q.device):
+        raise RuntimeError(f"gemm: out must be a contiguous bf16 [{M}, {N}] tensor on {a_q.device}")
     if requant and not write_d:
         d = None
     else:
