@@ -425,3 +425,15 @@ def test_staged_epilogue_combinations(cuda_device, M, N, K, gelu, requant, write
     else:
         d = res
     _check(d, ref)
+
+
+def test_gemm_rejects_bad_out(cuda_device):
+    from ltx_kernels.blockwise import ops
+    M, N, K = 64, 256, 256
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=77)
+    for bad in (torch.empty(M, N - 128, dtype=torch.bfloat16, device=cuda_device),
+                torch.empty(M, N, dtype=torch.float32, device=cuda_device),
+                torch.empty(N, M, dtype=torch.bfloat16, device=cuda_device).t(),
+                torch.empty(M, N, dtype=torch.bfloat16)):
+        with pytest.raises(RuntimeError):
+            ops.gemm(aq, asc, wq, wsc, b, out=bad)
