@@ -5,15 +5,17 @@ Default workload (the DiT FFN pair at M=24576 tokens per
     requant fused) -> down GEMM 16384->4096 (+bias, bf16 out).
 One "step" is that chain on one batch.  `value` is whole-job TFLOP/s (2*M*N*K per
 GEMM, summed over ranks), timed with CUDA events on the launching stream with
-inputs resident in HBM; `e2e` is the same metric through the public API with the
-input copied from pinned host memory and the output copied back every step.
+inputs resident in HBM; `e2e` is the same metric through the public layer modules
+with the input copied from pinned host memory and the output copied back every
+step, streamed in `--e2e-chunk` token chunks (ltx_kernels.blockwise.host_stream).
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
                     [--workload ffn|linear|qkv_lora|dit_step|producers]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--e2e-chunk T] [--m TOKENS]
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own token shard
-(weights replicated, no collective on the data path) -> "scaling": "weak".
+(weights replicated, no collective on the data path) -> "scaling": "weak" for the
+single-layer workloads; `dit_step` splits one step's tokens across ranks ("strong").
 `--impl reference` times the reference's CPU path (dequantise, fp32 matmul) as
 restated by the oracle, on a bounded sample of the same workload, on rank 0.
 """
