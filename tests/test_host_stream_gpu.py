@@ -92,3 +92,20 @@ def test_stream_rejects_bad_buffers(cuda_device):
         st(torch.zeros(10, 128, dtype=torch.bfloat16), torch.zeros(10, 256, dtype=torch.bfloat16))
     with pytest.raises(RuntimeError):
         st(torch.zeros(10, 256, dtype=torch.bfloat16), torch.zeros(9, 256, dtype=torch.bfloat16))
+
+
+def test_stream_with_split_k_chunks(cuda_device):
+    """Chunks small enough to take split-K with another split count than the whole batch:
+    rows agree with the whole-batch result to fp32 summation order."""
+    from ltx_kernels.blockwise import TokenStreamer, ops
+    K, N, rows, chunk = 4096, 1024, 640, 128
+    lin = _linear(K, N, cuda_device, 21)
+    assert ops.gemm_plan(chunk, N, K, cuda_device)["splits"] != ops.gemm_plan(rows, N, K, cuda_device)["splits"]
+    x = activations(rows, K, seed=21)
+    with torch.inference_mode():
+        ref = lin(x.to(cuda_device)[None])[0].float().cpu()
+        out = torch.empty(rows, N, dtype=torch.bfloat16).pin_memory()
+        TokenStreamer(lin, K, chunk, cuda_device)(x.pin_memory(), out)
+        torch.cuda.synchronize()
+    diff = (out.float() - ref).abs().max().item()
+    assert diff <= 0.02 * ref.abs().max().item()
