@@ -16,9 +16,11 @@
 //   * warp 0  TMA producer (both CTAs); warp 1  TMEM allocation (both CTAs) and
 //     MMA issue (leader CTA only); warps 4-11  per-128-K promotion of the TMEM
 //     partials into fp32 registers (one row, 128 columns per thread), then
-//     bf16(acc + bias) into a 64 KB shared staging tile; warps 2-3  drain the
-//     staging tile to global memory (plain store, or GELU-tanh + 1x128 requant)
-//     while the promotion warps already work on the next tile.
+//     y = bf16(acc + bias) (GELU-tanh applied when fused) and its 1x128 group
+//     abs-max into a 64 KB shared staging tile; warps 2-3  drain the staging
+//     tile with TMA stores (bf16 D and/or the requantised e4m3 codes) while the
+//     promotion warps already work on the next tile.  Epilogue and staging layout
+//     are those of the one-CTA kernel, per CTA over its 128 rows.
 #pragma once
 
 #include "gemm.cuh"
@@ -42,10 +44,12 @@ constexpr int kScaleRing = 4;  // K blocks of scales in flight per promotion thr
 // Per promotion thread: kScaleRing slots of (sfa, sfb), slot-major so that a
 // warp's 32 lanes read 32 consecutive words.
 constexpr uint32_t kScaleRingBytes = 256 * kScaleRing * 2 * 4;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + kStagingBytes + kScaleRingBytes + 1024 + 256;
+constexpr uint32_t kStagingAmaxBytes = 2 * kRowsPerCta * 4;  // abs-max per (128-column half, row)
+constexpr uint32_t kSmemBytes =
+    kStages * kStageBytes + kStagingBytes + kStagingAmaxBytes + kScaleRingBytes + 1024 + 256;
 
-constexpr uint32_t kRegsCtrl = 56;   // warps 0-3: producer, MMA, store/GELU warps
-constexpr uint32_t kRegsEpi = 224;   // warps 4-11: promotion
+constexpr uint32_t kRegsCtrl = 40;   // warps 0-3: producer, MMA, store warps
+constexpr uint32_t kRegsEpi = 232;   // warps 4-11: promotion
 constexpr uint32_t kLaunchRegs = 168;
 static_assert(128 * kRegsCtrl + 256 * kRegsEpi <= kThreads * kLaunchRegs, "register split exceeds launch");
 
@@ -63,16 +67,10 @@ struct Params {
   GemmParams g;  // m_tiles / n_tiles / total_tiles count 256 x 256 pair tiles here
 };
 
-// Staging tile: row r (0..127) of 256 bf16 = 32 chunks of 16 B; chunk c is kept
-// at position c ^ (r & 7) so that 32 rows written at one column and one row read
-// across its columns both hit distinct banks.
-__device__ __forceinline__ uint32_t staging_off(int r, int chunk) {
-  return static_cast<uint32_t>(r) * 512u + static_cast<uint32_t>((chunk ^ (r & 7)) * 16);
-}
 
-// acc += scale * partial for one K block, 128 columns read as four 32-column
-// TMEM loads; the TMEM buffer is released on the leader's barrier after the
-// last load.
+// acc += scale * partial for one K block, 128 columns read in two TMEM round
+// trips of 64; the TMEM buffer is released on the leader's barrier after the
+// second one, before the last 32 packed FMAs.
 __device__ __forceinline__ bool promote_pair(uint64_t* tfull, uint32_t tempty_leader, uint32_t tmem_base, int sp,
                                              int half, uint32_t it, float scale, int lane, float2 (&acc)[64]) {
   const uint32_t buf = it & 1u, bph = (it >> 1) & 1u;
@@ -80,40 +78,42 @@ __device__ __forceinline__ bool promote_pair(uint64_t* tfull, uint32_t tempty_le
   tc_fence_after_sync();
   const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + buf * kTileN + half * 128;
   const float2 s2 = make_float2(scale, scale);
+  uint32_t r0[32], r1[32];
+  tmem_ld_32x32b_x32(taddr + 0, r0);
+  tmem_ld_32x32b_x32(taddr + 32, r1);
+  tmem_wait_ld();
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(taddr + 32 * c, r);
-    tmem_wait_ld();
-    if (c == 3) {
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader + buf * 8u);
-    }
+  for (int j = 0; j < 16; ++j) {
+    acc[j] = __ffma2_rn(s2, make_float2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1])), acc[j]);
+    acc[16 + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1])), acc[16 + j]);
+  }
+  tmem_ld_32x32b_x32(taddr + 64, r0);
+  tmem_ld_32x32b_x32(taddr + 96, r1);
+  tmem_wait_ld();
+  tc_fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive_cluster(tempty_leader + buf * 8u);
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      acc[16 * c + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])),
-                                   acc[16 * c + j]);
+  for (int j = 0; j < 16; ++j) {
+    acc[32 + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1])), acc[32 + j]);
+    acc[48 + j] = __ffma2_rn(s2, make_float2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1])), acc[48 + j]);
   }
   return true;
 }
 
-// 8 bf16 (one 16 B chunk) -> GELU-tanh in fp32, rounded back to bf16 values.
-__device__ __forceinline__ void gelu8(float (&f)[8]) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = bf16_round(gelu_tanh_f32(f[i]));
-}
 
 template <bool kGelu, bool kRequant>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_blockwise_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                    const __grid_constant__ CUtensorMap tmLX, const __grid_constant__ CUtensorMap tmLB,
+                                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmQ,
                                    const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* staging = smem + kStages * kStageBytes;
-  uint8_t* scale_ring = staging + kStagingBytes;
+  float* stg_amax = reinterpret_cast<float*>(staging + kStagingBytes);  // [2 halves][128 rows]
+  uint8_t* scale_ring = staging + kStagingBytes + kStagingAmaxBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(scale_ring + kScaleRingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;  // [2]
@@ -151,6 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmLX);
       tma_prefetch_desc(&tmLB);
     }
+    if (p.flags & kGemmWriteD) tma_prefetch_desc(&tmD);
+    if (kRequant) tma_prefetch_desc(&tmQ);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -244,77 +246,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= 2) {
       // ------------------------------------------------------------ staging -> global (warps 2, 3)
       // (Only whole warps 2 and 3 enter: lanes 1-31 of warp 0 must not, their
-      // lane 0 is the producer and never joins these warp-wide votes.)
+      // lane 0 is the producer and never joins these warp-wide votes.)  As in the
+      // one-CTA kernel: warp pw owns the 32-row slices pw*32 and 64 + pw*32 of this
+      // CTA's 128 rows; lane 0 issues the TMA stores.
       const int pw = warp - 2;  // 0 or 1
+      const bool write_d = (p.flags & kGemmWriteD) != 0;
       uint32_t tcount = 0;
-      bool ok = true;
-      for (int tile = cluster_id; tile < p.total_tiles && ok; tile += num_clusters, ++tcount) {
+      for (int tile = cluster_id; tile < p.total_tiles; tile += num_clusters, ++tcount) {
         int mt, nt;
         gemm_tile_coords(tile, p, mt, nt);
         const int m0 = mt * kTileM + static_cast<int>(rank) * kRowsPerCta;
         const int n0 = nt * kTileN;
-        if (!__all_sync(0xffffffffu, mbar_wait(stg_full, tcount & 1u, kStPStagingFull))) {
-          ok = false;
-          break;
-        }
-        if constexpr (!kGelu && !kRequant) {
-          // Plain: each warp instruction writes one full 512 B output row.
-          for (int r = pw; r < kRowsPerCta; r += 2) {
-            const int row = m0 + r;
-            const uint4 v = *reinterpret_cast<const uint4*>(staging + staging_off(r, lane));
-            const int col = n0 + lane * 8;
-            if (row < p.M && col < p.N)
-              *reinterpret_cast<uint4*>(p.d + static_cast<int64_t>(row) * p.N + col) = v;
+        if (!__all_sync(0xffffffffu, mbar_wait(stg_full, tcount & 1u, kStPStagingFull))) break;
+        if constexpr (kRequant) {
+#pragma unroll 1
+          for (int j = 0; j < 4; ++j) {
+            const int g = j & 1;
+            const int rb = (j >> 1) * 64 + pw * 32;
+            const int r = rb + lane;
+            const int col0 = n0 + g * 128;
+            if (col0 >= p.N) continue;  // warp-uniform: N % 128 == 0
+            const bool slice_ok = m0 + rb < p.M;
+            if (write_d) {
+              if (lane == 0 && slice_ok) {
+                tma_store_2d(&tmD, staging + (2 * g) * kStagingBlockBytes + rb * 128, col0, m0 + rb);
+                tma_store_2d(&tmD, staging + (2 * g + 1) * kStagingBlockBytes + rb * 128, col0 + 64, m0 + rb);
+                tma_store_commit();
+                tma_store_wait_read();  // the codes below overwrite the slice
+              }
+              __syncwarp();
+            }
+            const float s = __fmul_rn(__frcp_rn(stg_amax[g * kRowsPerCta + r]), 448.0f);
+            const bool in_range = isfinite(s);  // then no product exceeds 448: plain hardware conversion
+            uint8_t* qrow = staging + (2 * g) * kStagingBlockBytes + r * 128;
+#pragma unroll 1
+            for (int k = 0; k < 8; ++k) {  // 16 codes from bf16 chunks 2k, 2k+1
+              uint32_t w4[4];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint4 v = *reinterpret_cast<const uint4*>(staging + gemm_staging_off(r, g * 16 + 2 * k + h));
+                float f[8];
+                bf16x8_to_f32(v, f);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  const float v0 = __fmul_rn(f[4 * i], s), v1 = __fmul_rn(f[4 * i + 1], s);
+                  const float v2 = __fmul_rn(f[4 * i + 2], s), v3 = __fmul_rn(f[4 * i + 3], s);
+                  const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+                  const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
+                  w4[2 * h + i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+                }
+              }
+              // Code chunk k replaces bf16 chunk k of the block, already read (k <= 2k).
+              *reinterpret_cast<uint4*>(qrow + ((k ^ (r & 7)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            if (m0 + r < p.M) p.s_out[static_cast<int64_t>(col0 / 128) * p.s_out_ld + m0 + r] = __frcp_rn(s);
+            __syncwarp();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && slice_ok) {
+              tma_store_2d(&tmQ, staging + (2 * g) * kStagingBlockBytes + rb * 128, col0, m0 + rb);
+              tma_store_commit();
+            }
           }
         } else {
-          // 1x128 groups: 16 lanes per group (8 values each); a warp covers two
-          // groups (both 128-column halves of one row) per step.
-          const int l16 = lane & 15, g = lane >> 4;
-          for (int r = pw; r < kRowsPerCta; r += 2) {
-            const int row = m0 + r;
-            const int chunk = g * 16 + l16;
-            const uint4 v = *reinterpret_cast<const uint4*>(staging + staging_off(r, chunk));
-            float f[8];
-            bf16x8_to_f32(v, f);
-            if constexpr (kGelu) gelu8(f);
-            const int col = n0 + chunk * 8;
-            const bool ok_out = row < p.M && col < p.N;
-            if (ok_out && (p.flags & kGemmWriteD)) {
-              *reinterpret_cast<uint4*>(p.d + static_cast<int64_t>(row) * p.N + col) =
-                  make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                             pack_bf16x2(f[6], f[7]));
+          // bf16 D (GELU already applied by the promotion warps), stored as staged.
+          if (lane == 0) {
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              const int rb = h * 64 + pw * 32;
+              if (m0 + rb >= p.M) continue;
+#pragma unroll 1
+              for (int b4 = 0; b4 < 4; ++b4)
+                if (n0 + b4 * 64 < p.N)
+                  tma_store_2d(&tmD, staging + b4 * kStagingBlockBytes + rb * 128, n0 + b4 * 64, m0 + rb);
             }
-            if constexpr (kRequant) {
-              float amax = 0.0f;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) amax = fmax_nan(amax, fabsf(f[i]));
-#pragma unroll
-              for (int off = 8; off > 0; off >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, off, 16));
-              const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
-              uint16_t c0, c1, c2, c3;
-              if (isfinite(s)) {
-                c0 = f32x2_to_e4m3x2_inrange(__fmul_rn(f[0], s), __fmul_rn(f[1], s));
-                c1 = f32x2_to_e4m3x2_inrange(__fmul_rn(f[2], s), __fmul_rn(f[3], s));
-                c2 = f32x2_to_e4m3x2_inrange(__fmul_rn(f[4], s), __fmul_rn(f[5], s));
-                c3 = f32x2_to_e4m3x2_inrange(__fmul_rn(f[6], s), __fmul_rn(f[7], s));
-              } else {
-                c0 = f32x2_to_e4m3x2(__fmul_rn(f[0], s), __fmul_rn(f[1], s));
-                c1 = f32x2_to_e4m3x2(__fmul_rn(f[2], s), __fmul_rn(f[3], s));
-                c2 = f32x2_to_e4m3x2(__fmul_rn(f[4], s), __fmul_rn(f[5], s));
-                c3 = f32x2_to_e4m3x2(__fmul_rn(f[6], s), __fmul_rn(f[7], s));
-              }
-              if (ok_out) {
-                *reinterpret_cast<uint2*>(p.q_out + static_cast<int64_t>(row) * p.N + col) =
-                    make_uint2(static_cast<uint32_t>(c0) | (static_cast<uint32_t>(c1) << 16),
-                               static_cast<uint32_t>(c2) | (static_cast<uint32_t>(c3) << 16));
-                if (l16 == 0) p.s_out[static_cast<int64_t>(col / 128) * p.s_out_ld + row] = __frcp_rn(s);
-              }
-            }
+            tma_store_commit();
           }
         }
+        // The staging tile may be overwritten once the stores have read it.
+        if (lane == 0) tma_store_wait_read();
         __syncwarp();
         if (lane == 0) mbar_arrive(stg_empty);
       }
+      if (lane == 0) tma_store_wait_all();
+      __syncwarp();
     }
   } else {
     setmaxnreg_inc<kRegsEpi>();
@@ -368,13 +383,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       cp_async_wait<0>();
       if (!ok) break;
 
-      // bf16(acc + bias) into the staging tile once the store warps have drained it.
+      // y = bf16(acc + bias) (+ GELU) into the staging tile once the store warps
+      // have drained it, and the group's abs-max for the requantisation.
       if (!__all_sync(0xffffffffu, mbar_wait(stg_empty, (tcount & 1u) ^ 1u, kStPStagingEmpty))) {
         ok = false;
         break;
       }
       const bool has_bias = (p.flags & kGemmBias) != 0 && col_ok;
       const float4* bias4 = reinterpret_cast<const float4*>(p.bias + col0);
+      float gmax = 0.0f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 columns
         float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
@@ -383,10 +400,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           b1 = __ldg(bias4 + 2 * c + 1);
         }
         const float2 a0 = acc[4 * c], a1 = acc[4 * c + 1], a2 = acc[4 * c + 2], a3 = acc[4 * c + 3];
-        const uint4 v = make_uint4(pack_bf16x2(a0.x + b0.x, a0.y + b0.y), pack_bf16x2(a1.x + b0.z, a1.y + b0.w),
-                                   pack_bf16x2(a2.x + b1.x, a2.y + b1.y), pack_bf16x2(a3.x + b1.z, a3.y + b1.w));
-        *reinterpret_cast<uint4*>(staging + staging_off(r_local, half * 16 + c)) = v;
+        uint32_t w4[4] = {pack_bf16x2(a0.x + b0.x, a0.y + b0.y), pack_bf16x2(a1.x + b0.z, a1.y + b0.w),
+                          pack_bf16x2(a2.x + b1.x, a2.y + b1.y), pack_bf16x2(a3.x + b1.z, a3.y + b1.w)};
+        if constexpr (kGelu) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 y =
+                gelu_tanh_f32x2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)));
+            w4[i] = pack_bf16x2(y.x, y.y);
+          }
+        }
+        if constexpr (kRequant) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            gmax = fmax_nan(gmax, fmax_nan(fabsf(__uint_as_float(w4[i] << 16)),
+                                           fabsf(__uint_as_float(w4[i] & 0xFFFF0000u))));
+        }
+        *reinterpret_cast<uint4*>(staging + gemm_staging_off(r_local, half * 16 + c)) =
+            make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
+      if constexpr (kRequant) stg_amax[half * kRowsPerCta + r_local] = gmax;
+      fence_proxy_async_smem();  // the store warps hand these bytes straight to TMA
       __syncwarp();
       if (lane == 0) mbar_arrive(stg_full);
     }

@@ -258,7 +258,8 @@ int gemm_launch_full(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, 
 
 template <bool kGelu, bool kRequant>
 int gemm_pair_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& lx,
-                     const CUtensorMap& lb, const GemmParams& p, cudaStream_t stream) {
+                     const CUtensorMap& lb, const CUtensorMap& md, const CUtensorMap& mq, const GemmParams& p,
+                     cudaStream_t stream) {
   auto kern = pair::fp8_blockwise_gemm_pair_kernel<kGelu, kRequant>;
   const int idx = (kGelu ? 1 : 0) | (kRequant ? 2 : 0);
   cudaLaunchConfig_t cfg;
@@ -296,7 +297,7 @@ int gemm_pair_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, 
   }
   const int clusters = p.total_tiles < d->pair_clusters ? p.total_tiles : d->pair_clusters;
   cfg.gridDim = dim3(2 * clusters);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, lx, lb, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, lx, lb, md, mq, p);
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
@@ -827,14 +828,9 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
   }
 
   const bool gelu = e.gelu_tanh != 0, requant = e.requant_q != nullptr;
-  if (use_pair) {
-    if (gelu && requant) return gemm_pair_launch<true, true>(d, ma, mb, mlx, mlb, p, stream);
-    if (gelu) return gemm_pair_launch<true, false>(d, ma, mb, mlx, mlb, p, stream);
-    if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, p, stream);
-    return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, p, stream);
-  }
-  // Output maps for the staged epilogue's TMA stores: bf16 D in [32, 64] boxes,
-  // e4m3 codes in [32, 128] boxes, 128 B swizzle (the staging tile's layout).
+  // Output maps for the staged epilogue's TMA stores (both kernels): bf16 D in
+  // [32, 64] boxes, e4m3 codes in [32, 128] boxes, 128 B swizzle (the staging
+  // tile's layout).
   CUtensorMap md = ma, mq = ma;
   if (!split) {
     if (write_d) {
@@ -845,6 +841,12 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
       rc = make_map_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.q_out, N, rows, N, 128, 32);
       if (rc) return rc;
     }
+  }
+  if (use_pair) {
+    if (gelu && requant) return gemm_pair_launch<true, true>(d, ma, mb, mlx, mlb, md, mq, p, stream);
+    if (gelu) return gemm_pair_launch<true, false>(d, ma, mb, mlx, mlb, md, mq, p, stream);
+    if (requant) return gemm_pair_launch<false, true>(d, ma, mb, mlx, mlb, md, mq, p, stream);
+    return gemm_pair_launch<false, false>(d, ma, mb, mlx, mlb, md, mq, p, stream);
   }
   if (gelu && requant) return gemm_launch_full<true, true>(d, ma, mb, mlx, mlb, md, mq, p, stream);
   if (gelu) return gemm_launch_full<true, false>(d, ma, mb, mlx, mlb, md, mq, p, stream);
