@@ -1,28 +1,41 @@
 """Benchmark of the B200 blockwise-FP8 linear path (BASELINE.json metric).
 
-Default workload (the DiT FFN pair at M=24576 tokens per GPU):
-    quantise x (bf16 [M, 4096]) -> up GEMM 4096->16384 (+bias, GELU-tanh, 1x128
-    requant fused) -> down GEMM 16384->4096 (+bias, bf16 out).
-One "step" is that chain on one batch.  `value` is whole-job TFLOP/s (2*M*N*K per
-GEMM, summed over ranks), timed with CUDA events on the launching stream with
-inputs resident in HBM; `e2e` is the same metric through the public layer modules
-with the input copied from pinned host memory and the output copied back every
-step, streamed in `--e2e-chunk` token chunks (ltx_kernels.blockwise.host_stream).
+BASELINE.json's metric is "FP8 blockwise GEMM TFLOPS & % B200 FP8 peak; DiT
+linear-stack ms at 1/2/4/8 GPU".  The default workload measures both halves:
+
+* the step: BASELINE config 3, one denoising step of the 48-block dual-stream DiT,
+  linears only, CFG batch 2 (28 blockwise-FP8 GEMMs per block), token-sharded over
+  the ranks with weights replicated (strong scaling: the step's tokens are split).
+  The step runs through the package's public layer modules (``BlockwiseFP8Linear``,
+  ``BlockwiseFP8FeedForward``) on the step's quantised token streams; it is captured
+  once as a CUDA graph and replayed.  `value` is the whole job's TFLOP/s, `ms_per_step`
+  the step time (max over ranks, CUDA events).
+* the GEMM: `headline_gemm` is the 24576 x 4096 -> 16384 up projection (bias +
+  GELU-tanh + 1x128 requant fused), the shape of BASELINE's >= 70 % target, event-timed
+  in isolation (burst) and over a seconds-long loop (sustained, clocks sampled).
+
+`e2e` is the same step with the step's bf16 token streams copied in from pinned host
+memory, quantised on the device, run through the stack, and the step's outputs (the
+last block's video and audio FFN outputs) copied back, every step.
+`gpu_reference` times the reference's own B200 path (its Triton 1x128 quantiser and
+its SM89 mma.sync GEMM with fp32 accumulation, built from the reference's sources
+into oracle/_ref) on config 0, config 1 and the headline GEMM, beside ours.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload ffn|linear|qkv_lora|dit_step|producers]
+                    [--workload dit_step|ffn|linear|qkv_lora|producers|sweep]
                     [--impl ours|reference] [--e2e-chunk T] [--m TOKENS]
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own token shard
-(weights replicated, no collective on the data path) -> "scaling": "weak" for the
-single-layer workloads; `dit_step` splits one step's tokens across ranks ("strong").
-`--impl reference` times the reference's CPU path (dequantise, fp32 matmul) as
-restated by the oracle, on a bounded sample of the same workload, on rank 0.
+Multi-GPU (torchrun, one process per GPU): every rank runs its token shard, no
+collective on the data path.  `--impl reference` times the reference's CPU torch
+path (blockwise_quantize_torch, dequantise, fp32 matmul, bias, bf16; the reference's
+own functions from oracle/_ref, else the oracle's restatement) on a bounded sample
+of the same workload, on rank 0.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -35,6 +48,7 @@ for _p in (os.path.join(REPO, "ltx-2_b200"), REPO):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+BASELINE_METRIC = "FP8 blockwise GEMM TFLOPS & % B200 FP8 peak; DiT linear-stack ms at 1/2/4/8 GPU"
 NOMINAL_FP8_TFLOPS = 4500.0
 
 WORKLOADS = {
@@ -75,6 +89,11 @@ DIT_BLOCK_GEMMS = [
     ("video", 4096, 2048, "bias", "v"), ("audio", 2048, 2048, "bias", "a"),  # video->audio q, k, v, out
 ]
 assert len(DIT_BLOCK_GEMMS) == 28
+# The step's input token streams: one bf16 tensor per (token class, width) a GEMM reads
+# (the FFN down projections read the up projections' requantised hidden state).
+DIT_INPUTS = sorted({(c, K) for c, K, N, e, s in DIT_BLOCK_GEMMS if not s.startswith("ffn")})
+
+HEADLINE = (24576, 4096, 16384)  # M, K, N of BASELINE's >= 70 % target (config-1 up projection)
 
 
 def _env_int(name, default):
@@ -82,6 +101,32 @@ def _env_int(name, default):
         return int(os.environ.get(name, default))
     except ValueError:
         return default
+
+
+# ----------------------------------------------------------------------------- peaks
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def fp8_peak(sustained: bool = False):
+    """Dense e4m3 tensor peak: twice the measured bf16 GEMM peak (the tensor core's e4m3
+    rate is twice its bf16 rate); fallback 2 x 1590 / 2 x 1400 TFLOP/s."""
+    mp = measured_peaks()
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    if key in mp:
+        return 2.0 * float(mp[key]), f"2 x MEASURED_PEAKS.json {key} (of measured)"
+    return (2800.0 if sustained else 3180.0), "2 x fallback bf16 (of fallback)"
+
+
+def hbm_peak():
+    mp = measured_peaks()
+    if "hbm_gbs" in mp:
+        return float(mp["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    return 6650.0, "fallback 6.65 TB/s (of fallback)"
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -106,6 +151,7 @@ class ClockSampler:
             self._t.start()
         except (OSError, ValueError):
             self.proc = None
+        return self
 
     def _read(self):
         for line in self.proc.stdout:
@@ -119,7 +165,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sm, smax, reasons = [], 0.0, set()
+        sm, smax, power, reasons = [], 0.0, [], set()
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
@@ -127,6 +173,7 @@ class ClockSampler:
             try:
                 sm.append(float(parts[1]))
                 smax = max(smax, float(parts[2]))
+                power.append(float(parts[3]))
             except ValueError:
                 continue
             for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
@@ -136,29 +183,578 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w_median": statistics.median(power) if power else None}
 
 
-# ----------------------------------------------------------------------------- workload
-def build_workload(name: str, M: int, dev, seed: int):
-    """Seeded synthetic inputs resident on `dev`: x bf16 ~N(0,1) with 1% outlier channels
-    x20; weights ~N(0,0.02) block-quantised by the library's weight kernel; bias ~N(0,0.01)."""
+# ----------------------------------------------------------------------------- timing helpers
+def _events():
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def time_launches(fn, reps: int, warmup: int = 3, flush=None):
+    """Mean device time (ms) of `fn` over `reps` launches, each bracketed by CUDA events on
+    the current stream; `flush()` (untimed) runs before each launch when given."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    evs = [_events() for _ in range(reps)]
+    for s, e in evs:
+        if flush is not None:
+            flush()
+        s.record()
+        fn()
+        e.record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in evs) / reps
+
+
+def time_loop(fn, seconds: float, gpu_index: int):
+    """Back-to-back launches of `fn` for about `seconds` (sustained regime, under the power
+    cap); returns (mean ms per launch, launches, clocks sampled meanwhile)."""
+    import torch
+    t = time_launches(fn, 3, warmup=2)
+    n = max(5, int(seconds * 1e3 / max(t, 1e-3)))
+    clk = ClockSampler(gpu_index).start()
+    s, e = _events()
+    s.record()
+    for _ in range(n):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / n, n, clk.stop()
+
+
+class L2Flush:
+    """Writes a buffer larger than the 126 MB L2 between timed launches of small shapes."""
+
+    def __init__(self, dev):
+        import torch
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+# ----------------------------------------------------------------------------- synthetic inputs
+def synth_acts(M: int, K: int, g, dev):
+    """bf16 ~N(0,1) with a seeded 1 % of channels x20 (BASELINE.json's activations)."""
+    import torch
+    x = torch.randn(M, K, generator=g, device=dev)
+    x[:, torch.randperm(K, generator=g, device=dev)[: max(1, K // 100)]] *= 20.0
+    return x.to(torch.bfloat16)
+
+
+def synth_weight(N: int, K: int, g, dev):
+    """~N(0, 0.02), block-quantised by the library's 128 x 128 weight kernel, plus a bias
+    ~N(0, 0.01) rounded to bf16 and held in fp32."""
     import torch
     from ltx_kernels.blockwise import ops
+    w = torch.randn(N, K, generator=g, device=dev) * 0.02
+    wq, ws = ops.quantize_weight_128x128(w)
+    del w
+    b = (torch.randn(N, generator=g, device=dev) * 0.01).to(torch.bfloat16).float()
+    return wq, ws, b
 
+
+def gemm_alg_bytes(M, K, N, epi) -> float:
+    """Algorithmic bytes of one GEMM launch: A + SFA + W + SFB + bias + output."""
+    b = M * K + 4 * M * K / 128 + N * K + 4 * N * K / 16384 + 4 * N
+    if epi == "gelu_requant":
+        b += M * N + 4 * M * N / 128
+    else:
+        b += 2 * M * N
+    if epi.startswith("lora"):
+        r = int(epi[4:])
+        b += 2 * M * r + 2 * N * r
+    return b
+
+
+def measure_cublas_fp8(dev) -> float | None:
+    """cuBLASLt e4m3 GEMM throughput (torch._scaled_mm, 8192^3, best of 10), TFLOP/s:
+    an external reference point (per-tensor scales, no block-scale promotion)."""
+    import torch
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=dev)
+        f = lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        best = min(time_launches(f, 1, warmup=0) for _ in range(10))
+        del a, b
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    except Exception:  # noqa: BLE001 - informational
+        return None
+
+
+# ----------------------------------------------------------------------------- the headline GEMM
+def headline_gemm(dev, gpu_index: int, sustained_s: float = 3.0) -> dict:
+    """The 24576 x 4096 -> 16384 up projection with bias + GELU-tanh + 1x128 requant fused:
+    burst (event-timed launches) and sustained (a seconds-long loop, clocks sampled)."""
+    import torch
+    from ltx_kernels.blockwise import ops
+    M, K, N = HEADLINE
+    g = torch.Generator(device=dev).manual_seed(77)
+    aq, asc = ops.quantize_1x128(synth_acts(M, K, g, dev))
+    wq, ws, b = synth_weight(N, K, g, dev)
+    f = lambda: ops.gemm(aq, asc, wq, ws, b, gelu=True, requant=True, write_d=False)
+    burst = time_launches(f, 10)
+    sus_ms, n, clk = time_loop(f, sustained_s, gpu_index)
+    flops = 2.0 * M * N * K
+    pk, pk_src = fp8_peak()
+    pks, pks_src = fp8_peak(sustained=True)
+    tf, tfs = flops / (burst * 1e-3) / 1e12, flops / (sus_ms * 1e-3) / 1e12
+    return {"shape": {"M": M, "K": K, "N": N, "epilogue": "bias + GELU-tanh + 1x128 requant"},
+            "kernel": "fp8_blockwise_gemm_kernel<1,1>",
+            "burst": {"ms": burst, "tflops": tf, "frac_of_fp8_peak": tf / pk, "peak": pk, "peak_source": pk_src,
+                      "frac_of_nominal_4500": tf / NOMINAL_FP8_TFLOPS},
+            "sustained": {"ms": sus_ms, "tflops": tfs, "launches": n, "frac_of_fp8_peak": tfs / pks, "peak": pks,
+                          "peak_source": pks_src, "clocks": clk},
+            "alg_bytes": gemm_alg_bytes(M, K, N, "gelu_requant")}
+
+
+# ----------------------------------------------------------------------------- the reference's GPU path
+def gpu_reference_record(dev) -> dict:
+    """The reference's own B200 path timed beside ours on identical inputs: its Triton 1x128
+    quantiser (triton_ops.py:102-151) and its SM89 mma.sync GEMM with fp32 accumulation
+    (linear.py:25-35,98-104; csrc/blockwise/kernels/geforce/gemm.cu), built for sm_100a
+    into oracle/_ref.  The reference's FFN runs GELU unfused (torch F.gelu on the bf16
+    GEMM output, gelu_approx.py:10) and re-quantises it with the Triton quantiser."""
+    import torch
+    import torch.nn.functional as F
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
+    from oracle import refpath
+    if not refpath.available():
+        return {"available": False, "why": "oracle/_ref not built (needs the reference checkout at build time)"}
+    G, T = refpath.gemm(), refpath.triton_ops()
+    out = {"available": True, "ref_path": "Triton quant + SM89 mma.sync GEMM (fp32 accumulate), sm_100a build",
+           "ours_path": "CUDA quant + tcgen05 GEMM (fused epilogue)"}
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def sm89(a, s, w, ws, b, M, N):
+        d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        G.fp8_gemm_nt_sm89((a, s), (w, ws), d, b, use_fast_accum=False)
+        return d
+
+    # headline GEMM shape, bf16 out + bias on both sides
+    M, K, N = HEADLINE
+    x = synth_acts(M, K, g, dev)
+    aq, asc = ops.quantize_1x128(x)
+    wq, ws, b = synth_weight(N, K, g, dev)
+    t_ref = time_launches(lambda: sm89(aq, asc, wq, ws, b, M, N), 5, warmup=2)
+    t_ours = time_launches(lambda: ops.gemm(aq, asc, wq, ws, b), 10)
+    fl = 2.0 * M * N * K
+    out["gemm_24576x4096x16384_bias_bf16"] = {"ref_ms": t_ref, "ours_ms": t_ours, "ref_tflops": fl / t_ref / 1e9,
+                                              "ours_tflops": fl / t_ours / 1e9, "speedup": t_ref / t_ours}
+    # config 1: the FFN pair at 24576 tokens
+    w2q, w2s, b2 = synth_weight(4096, 16384, g, dev)
+
+    def ref_ffn():
+        q, s = T._quant_blockwise_tma_aligned_func(x.view(1, M, K), False)
+        h = F.gelu(sm89(q.view(M, K), s, wq, ws, b, M, N), approximate="tanh")
+        hq, hs = T._quant_blockwise_tma_aligned_func(h.view(1, M, N), False)
+        return sm89(hq.view(M, N), hs, w2q, w2s, b2, M, 4096)
+
+    def our_ffn():
+        q, s = ops.quantize_1x128(x, L.QUANT_TRITON)
+        _, hq, hs = ops.gemm(q, s, wq, ws, b, gelu=True, requant=True, write_d=False)
+        return ops.gemm(hq, hs, w2q, w2s, b2)
+
+    t_ref, t_ours = time_launches(ref_ffn, 3, warmup=1), time_launches(our_ffn, 10)
+    fl = 2 * 2.0 * M * N * K
+    out["ffn_config1"] = {"ref_ms": t_ref, "ours_ms": t_ours, "ref_tflops": fl / t_ref / 1e9,
+                          "ours_tflops": fl / t_ours / 1e9, "speedup": t_ref / t_ours}
+    del w2q, w2s
+    # config 0: quantise + one 6144 x 4096 -> 4096 linear
+    M0, K0, N0 = 6144, 4096, 4096
+    x0 = synth_acts(M0, K0, g, dev)
+    w0q, w0s, b0 = synth_weight(N0, K0, g, dev)
+    flush = L2Flush(dev)
+
+    def ref_lin():
+        q, s = T._quant_blockwise_tma_aligned_func(x0.view(1, M0, K0), False)
+        return sm89(q.view(M0, K0), s, w0q, w0s, b0, M0, N0)
+
+    def our_lin():
+        q, s = ops.quantize_1x128(x0, L.QUANT_TRITON)
+        return ops.gemm(q, s, w0q, w0s, b0)
+
+    t_ref, t_ours = time_launches(ref_lin, 10, flush=flush), time_launches(our_lin, 10, flush=flush)
+    fl = 2.0 * M0 * N0 * K0
+    out["linear_config0"] = {"ref_ms": t_ref, "ours_ms": t_ours, "ref_tflops": fl / t_ref / 1e9,
+                             "ours_tflops": fl / t_ours / 1e9, "speedup": t_ref / t_ours, "l2": "flushed"}
+    torch.cuda.synchronize()
+    return out
+
+
+# ----------------------------------------------------------------------------- CPU reference path
+def _cpu_threads() -> int:
+    import torch
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def cpu_reference_layers(layers, rows: int, seed: int = 0, budget_s: float = 8.0):
+    """The reference's CPU torch path over `rows` tokens of a stack of linears, each
+    (K, N, epilogue, input key): blockwise_quantize_torch (functional.py:138-144) of the
+    bf16 input, dequantise, fp32 matmul with the dequantised blockwise_quantize_weights
+    weight (functional.py:128-135, load time, untimed), + fp32 bias, bf16; GELU-tanh in
+    torch on bf16 after a gelu_requant layer.  The reference's own functions come from
+    oracle/_ref (kind "reference"); without it, the oracle's restatement (kind "port").
+    Returns (seconds per pass, flops per pass, threads, kind)."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+    from oracle import refpath
+
+    threads = _cpu_threads()
+    g = torch.Generator().manual_seed(seed)
+    if refpath.available("py"):
+        RF = refpath.functional(with_cuda_ops=False)
+        kind = "reference"
+
+        def quant(x):  # x bf16 [M, K] -> (e4m3 [M, K], scales [K/128, M])
+            q, s = RF.blockwise_quantize_torch(x.view(1, *x.shape))
+            return q.view(x.shape), s
+
+        def wquant(w):
+            return RF.blockwise_quantize_weights(w)
+    else:
+        from oracle import oracle as O
+        kind = "port"
+
+        def quant(x):
+            xb = x.contiguous().view(torch.int16).numpy().view(np.uint16)
+            q, s = O.quant_act_1x128(xb)
+            return torch.from_numpy(q).view(torch.float8_e4m3fn), torch.from_numpy(s[:, : x.shape[0]].copy())
+
+        def wquant(w):
+            q, s = O.quant_weight_128x128(w.numpy())
+            return torch.from_numpy(q).view(torch.float8_e4m3fn), torch.from_numpy(s)
+
+    def dequant_act(q, s):
+        M, K = q.shape
+        return (q.float().view(M, K // 128, 128) * s.t().reshape(M, K // 128, 1)).view(M, K)
+
+    mats, inputs = [], {}
+    for K, N, epi, key in layers:
+        wq, ws = wquant(torch.randn(N, K, generator=g) * 0.02)
+        wd = (wq.float().view(N // 128, 128, K // 128, 128) * ws.view(N // 128, 1, K // 128, 1)).view(N, K)
+        b = (torch.randn(N, generator=g) * 0.01).to(torch.bfloat16).float()
+        mats.append((K, N, epi, key, wd, b))
+        if key is not None and key not in inputs:
+            x = torch.randn(rows, K, generator=g)
+            x[:, torch.randperm(K, generator=g)[: max(1, K // 100)]] *= 20.0
+            inputs[key] = x.to(torch.bfloat16)
+
+    def run():
+        hidden = None
+        for K, N, epi, key, wd, b in mats:
+            x = hidden if key is None else inputs[key]
+            q, s = quant(x)
+            d = (dequant_act(q, s) @ wd.t() + b).to(torch.bfloat16)
+            hidden = F.gelu(d, approximate="tanh") if epi == "gelu_requant" else d
+
+    run()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 50:
+            break
+    flops = sum(2.0 * rows * N * K for K, N, epi, key, wd, b in mats)
+    return el / reps, flops, threads, kind
+
+
+def dit_cpu_layers():
+    """One DiT block as (K, N, epilogue, input key) for cpu_reference_layers; an FFN
+    down projection reads the preceding up projection's output (key None)."""
+    return [(K, N, e, None if s.startswith("ffn") else (c, K)) for c, K, N, e, s in DIT_BLOCK_GEMMS]
+
+
+def _dit_cpu_run(layers, rows: dict):
+    """One config-3 block through the reference CPU path: each token class's GEMMs as one
+    stack on `rows[class]` tokens (an FFN down projection reads its up projection's
+    output).  Returns (seconds per block, threads, kind)."""
+    total_t, threads, kind = 0.0, 1, "port"
+    for seed, cls in enumerate(("video", "audio", "text")):
+        sub = [lay for lay, (c, *_rest) in zip(layers, DIT_BLOCK_GEMMS) if c == cls]
+        per, _, threads, kind = cpu_reference_layers(sub, rows[cls], seed=seed, budget_s=4.0)
+        total_t += per
+    return total_t, threads, kind
+
+
+def dit_flops(toks: dict, blocks: int) -> float:
+    return blocks * sum(2.0 * toks[c] * K * N for c, K, N, _, _ in DIT_BLOCK_GEMMS)
+
+
+# ----------------------------------------------------------------------------- DiT step
+def dit_tokens_per_rank(world: int, scaling: str) -> dict:
+    """Token rows of each class on one rank: strong scaling splits the fixed step
+    (padded up to a multiple of the world size), weak scaling keeps the full step per rank."""
+    if scaling == "weak":
+        return dict(DIT_TOKENS)
+    return {k: -(-v // world) for k, v in DIT_TOKENS.items()}
+
+
+def build_dit_step(dev, world: int, rank: int, scaling: str, blocks: int = DIT_BLOCKS):
+    """The config-3 linear stack on this rank as the package's public layer modules.
+
+    Returns (step, xin, flops, launches, desc, toks): `xin` holds the step's bf16 input
+    token streams (one per (class, width) in DIT_INPUTS, device-resident); `step()`
+    quantises them (torch.ops.blockwise.quantize, the reference's op) and runs the
+    48 blocks, returning the last block's FFN outputs {"video": .., "audio": ..}."""
+    import torch
+    from ltx_kernels.blockwise import BlockwiseFP8FeedForward, BlockwiseFP8Linear
+    from ltx_kernels.blockwise import ops
+
+    toks = dit_tokens_per_rank(world, scaling)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    xin = {key: synth_acts(toks[key[0]], key[1], g, dev) for key in DIT_INPUTS}
+
+    def linear(K, N):
+        wq, ws, b = synth_weight(N, K, g, dev)
+        m = BlockwiseFP8Linear(K, N, bias=True, device=dev)
+        m.weight.data, m.weight_scale.data, m.bias.data = wq, ws, b
+        return m
+
+    layers = []
+    for _ in range(blocks):
+        blk, pending = [], None
+        for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
+            if epi == "gelu_requant":
+                pending = (cls, K, linear(K, N))
+            elif src.startswith("ffn"):
+                up_cls, up_K, up = pending
+                blk.append(("ffn", up_cls, up_K, BlockwiseFP8FeedForward.from_linears(up, linear(K, N))))
+            else:
+                blk.append(("linear", cls, K, linear(K, N)))
+        layers.append(blk)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        acts = {}
+        for (cls, K), x in xin.items():
+            q, s = torch.ops.blockwise.quantize(x.view(1, *x.shape), False)
+            acts[(cls, K)] = (q, s)
+        outs = {}
+        with torch.inference_mode():
+            for blk in layers:
+                for kind, cls, K, mod in blk:
+                    y = mod(acts[(cls, K)])
+                    if kind == "ffn":
+                        outs[cls] = y
+        return outs
+
+    flops = dit_flops(toks, blocks)
+    desc = (f"DiT linear stack (BASELINE config 3): {blocks} blocks x 28 FP8 GEMMs, CFG batch 2, tokens per rank "
+            f"video {toks['video']} / audio {toks['audio']} / text {toks['text']} ({scaling} scaling)")
+    launches = len(DIT_INPUTS)  # the step's quantiser launches
+    for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
+        launches += blocks * ops.gemm_plan(toks[cls], N, K, dev)["launches"]
+    return step, xin, flops, launches, desc, toks
+
+
+def dominant_kernel_roofline(dev, M: int, K: int = 4096, N: int = 16384) -> dict:
+    """The step's dominant kernel -- the video FFN up projection (bias + GELU + requant) at
+    this rank's token count -- event-timed in isolation in the same run."""
+    import torch
+    from ltx_kernels.blockwise import ops
+    g = torch.Generator(device=dev).manual_seed(78)
+    aq, asc = ops.quantize_1x128(synth_acts(M, K, g, dev))
+    wq, ws, b = synth_weight(N, K, g, dev)
+    flush = L2Flush(dev) if M * K + N * K < (126 << 20) else None
+    ms = time_launches(lambda: ops.gemm(aq, asc, wq, ws, b, gelu=True, requant=True, write_d=False), 10,
+                       flush=flush)
+    flops = 2.0 * M * N * K
+    pk, src = fp8_peak()
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
+            tr = json.load(f).get("ffn:gemm_4096x16384_gelu_requant")
+        if tr:  # captured at 24576 rows; scaled by rows processed
+            traffic = tr["bytes_per_launch_at_bench_size"] * M / 24576.0
+    except (OSError, ValueError, KeyError):
+        traffic = None
+    return {"bound": "tensor", "kernel": f"fp8_blockwise_gemm_kernel<1,1> (video FFN up, {M}x{K}->{N})",
+            "achieved": achieved, "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk, "peak_source": src,
+            "frac_of_nominal_4500": achieved / NOMINAL_FP8_TFLOPS, "launch_ms": ms,
+            "alg_bytes": gemm_alg_bytes(M, K, N, "gelu_requant"), "traffic": traffic,
+            "traffic_note": "ncu DRAM bytes of the 24576-row launch scaled by rows" if traffic else None,
+            "timing": "isolated launches, CUDA events on the launching stream" + (", L2 flushed" if flush else "")}
+
+
+def run_dit(args, rank: int, world: int, local: int):
+    """Config 3: the DiT linear stack, token-sharded over the ranks (strong scaling by default)."""
+    scaling = args.scaling or "strong"
+    sample = {"video": 512, "audio": 64, "text": 64}
+    toks_rank = dit_tokens_per_rank(world, scaling)
+    desc = (f"DiT linear stack (BASELINE config 3): {args.blocks} blocks x 28 FP8 GEMMs, CFG batch 2, tokens per "
+            f"rank video {toks_rank['video']} / audio {toks_rank['audio']} / text {toks_rank['text']} "
+            f"({scaling} scaling)")
+    cfg = {"workload": desc, "tokens_per_rank": toks_rank, "blocks": args.blocks,
+           "parallelism": f"token-sharded over {world} GPU(s), weights replicated, no collective",
+           "l2": "per-block weights 385 MB > L2; no flush"}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        per, threads, kind = _dit_cpu_run(dit_cpu_layers(), sample)
+        fl_sample = dit_flops(sample, 1)
+        val = fl_sample / per / 1e12
+        total = dit_flops(DIT_TOKENS, args.blocks)
+        print(json.dumps({
+            "metric": BASELINE_METRIC, "value": val, "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total / (val * 1e12) * 1e3, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32 (dequantised e4m3 operands)", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                             "sample": f"one of {args.blocks} blocks, tokens per class {sample}; the reference's "
+                                       "CPU torch path (blockwise_quantize_torch, dequantise, fp32 matmul, bias, "
+                                       "bf16, torch GELU); ms_per_step extrapolated to the full step by FLOPs"},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    import torch.distributed as dist
+    from ltx_kernels.blockwise import ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    step, xin, flops, launches, desc, toks = build_dit_step(dev, world, rank, scaling, args.blocks)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    assert ops.device_status() == 0
+    # The step is ~1350 launches; at several GPUs most of them are shorter than the
+    # host's per-call overhead, so the whole step is captured once as a CUDA graph (the
+    # C ABI neither allocates nor synchronises) and replayed.
+    graph, outs = None, None
+    if not args.no_graph:
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = step()
+        for _ in range(2):
+            graph.replay()
+        barrier()
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+            return outs
+        return step()
+
+    clocks = ClockSampler(local).start()
+    barrier()
+    t0, t1 = _events()
+    t0.record()
+    for _ in range(args.steps):
+        run_step()
+    t1.record()
+    barrier()
+    elapsed = t0.elapsed_time(t1)
+    clk = clocks.stop()
+
+    # End to end: this rank's bf16 token streams come from pinned host memory into the
+    # step's input buffers, are quantised and run through the stack on the device, and the
+    # step's outputs (last block's video and audio FFN outputs) return to pinned host memory.
+    hosts = {key: x.cpu().pin_memory() for key, x in xin.items()}
+    last = run_step()
+    out_host = {c: torch.empty(t.shape, dtype=t.dtype).pin_memory() for c, t in last.items()}
+
+    def e2e_step():
+        for key, h in hosts.items():
+            xin[key].copy_(h, non_blocking=True)
+        o = run_step()
+        for c, t in o.items():
+            out_host[c].copy_(t, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0, e1 = _events()
+    e2e_steps = max(1, min(args.steps, 3))
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    assert ops.device_status() == 0
+    if world > 1:
+        t = torch.tensor([elapsed, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, e2e_ms = t.tolist()
+    ms = elapsed / args.steps
+    total_flops = dit_flops(DIT_TOKENS, args.blocks) if scaling == "strong" else flops * world
+    value = total_flops / (ms * 1e-3) / 1e12
+    h2d = sum(h.numel() * h.element_size() for h in hosts.values())
+    d2h = sum(h.numel() * h.element_size() for h in out_host.values())
+    del graph, outs, last
+    torch.cuda.synchronize(dev)
+    # Per-rank extras (every rank runs them, so the collectives stay in step).
+    roof = dominant_kernel_roofline(dev, toks["video"])
+    head = headline_gemm(dev, local) if (world == 1 and not args.no_extras) else None
+    gref = gpu_reference_record(dev) if (world == 1 and not args.no_extras) else None
+    cublas = measure_cublas_fp8(dev) if (rank == 0 and not args.no_extras) else None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            per, threads, kind = _dit_cpu_run(dit_cpu_layers(), sample)
+            cpu = {"value": dit_flops(sample, 1) / per / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                   "sample": f"one block, tokens per class {sample}; the reference's CPU torch path"}
+        print(json.dumps({
+            "metric": BASELINE_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out",
+            "data": "synthetic (seeded; BASELINE.json distributions)", "config": cfg,
+            "dit_step_ms": ms,
+            "headline_gemm": head,
+            "roofline": roof,
+            "cublas_fp8_tflops": cublas,
+            "gpu_reference": gref,
+            "cpu_baseline": cpu,
+            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "H2D of the step's bf16 token streams into the step's input buffers, "
+                           "torch.ops.blockwise.quantize + BlockwiseFP8Linear / BlockwiseFP8FeedForward "
+                           "(graph-replayed), D2H of the last block's video and audio outputs"},
+            "gpu_launches": args.steps * launches,
+            "cuda_graph": not args.no_graph,
+            "clocks": clk,
+        }))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- single-layer workloads
+def build_workload(name: str, M: int, dev, seed: int):
+    """Seeded synthetic inputs resident on `dev` (BASELINE.json distributions)."""
+    import torch
     desc, _, layers = WORKLOADS[name]
     g = torch.Generator(device=dev).manual_seed(seed)
-    K0 = layers[0][0]
-    x = torch.randn(M, K0, generator=g, device=dev, dtype=torch.float32)
-    ch = torch.randperm(K0, generator=g, device=dev)[: max(1, K0 // 100)]
-    x[:, ch] *= 20.0
-    x = x.to(torch.bfloat16)
+    x = synth_acts(M, layers[0][0], g, dev)
     params = []
     for K, N, epi in layers:
-        w = torch.randn(N, K, generator=g, device=dev, dtype=torch.float32) * 0.02
-        wq, ws = ops.quantize_weight_128x128(w)
-        del w
-        b = (torch.randn(N, generator=g, device=dev) * 0.01).to(torch.bfloat16).float()
+        wq, ws, b = synth_weight(N, K, g, dev)
         lora = None
         if epi.startswith("lora"):
             r = int(epi[4:])
@@ -203,7 +799,6 @@ def build_module(name: str, params, dev):
 
 def make_step(x, params):
     """Returns step(events=None) running the workload once on the current stream."""
-    import torch
     from ltx_kernels.blockwise import ops
 
     def step(ev=None):
@@ -247,226 +842,32 @@ def kernel_names(name: str):
     return names
 
 
-def gemm_alg_bytes(M, K, N, epi) -> float:
-    """Algorithmic bytes of one GEMM launch: A + SFA + W + SFB + bias + output."""
-    b = M * K + 4 * M * K / 128 + N * K + 4 * N * K / 16384 + 4 * N
-    if epi == "gelu_requant":
-        b += M * N + 4 * M * N / 128
-    else:
-        b += 2 * M * N
-    if epi.startswith("lora"):
-        r = int(epi[4:])
-        b += 2 * M * r + 2 * N * r
-    return b
+def single_cpu_layers(name: str):
+    layers = WORKLOADS[name][2]
+    out = []
+    for i, (K, N, epi) in enumerate(layers):
+        out.append((K, N, "gelu_requant" if epi == "gelu_requant" else "bias", ("x", K) if i == 0 else None))
+    return out
 
 
-def measure_fp8_peak(dev) -> float | None:
-    """cuBLASLt e4m3 GEMM throughput (torch._scaled_mm, 8192^3, best of 10) in TFLOP/s."""
-    import torch
-    try:
-        n = 8192
-        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
-        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
-        one = torch.ones((), device=dev)
-        for _ in range(3):
-            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
-        best = None
-        for _ in range(10):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
-            e.record()
-            e.synchronize()
-            t = s.elapsed_time(e)
-            best = t if best is None else min(best, t)
-        del a, b
-        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
-    except Exception:  # noqa: BLE001 - the peak probe is informational
-        return None
-
-
-def dit_tokens_per_rank(world: int, scaling: str) -> dict:
-    """Token rows of each class on one rank: strong scaling splits the fixed step
-    (padded up to a multiple of the world size), weak scaling keeps the full step per rank."""
-    if scaling == "weak":
-        return dict(DIT_TOKENS)
-    return {k: -(-v // world) for k, v in DIT_TOKENS.items()}
-
-
-def build_dit_step(dev, world: int, rank: int, scaling: str, blocks: int = DIT_BLOCKS):
-    """Resident inputs and FP8 weights for the config-3 linear stack on this rank."""
-    import torch
-    from ltx_kernels.blockwise import ops
-
-    toks = dit_tokens_per_rank(world, scaling)
-    g = torch.Generator(device=dev).manual_seed(4321 + rank)
-    acts = {}
-
-    def act(cls, K):
-        key = (cls, K)
-        if key not in acts:
-            x = torch.randn(toks[cls], K, generator=g, device=dev)
-            x[:, torch.randperm(K, generator=g, device=dev)[: K // 100]] *= 20.0
-            acts[key] = ops.quantize_1x128(x.to(torch.bfloat16))
-        return acts[key]
-
-    layers = []
-    for _ in range(blocks):
-        blk = []
-        for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
-            w = torch.randn(N, K, generator=g, device=dev) * 0.02
-            wq, ws = ops.quantize_weight_128x128(w)
-            del w
-            b = (torch.randn(N, generator=g, device=dev) * 0.01).to(torch.bfloat16).float()
-            blk.append((cls, K, N, epi, src, wq, ws, b, None if src.startswith("ffn") else act(cls, K)))
-        layers.append(blk)
-    torch.cuda.synchronize(dev)
-
-    def step(ev=None):
-        hidden = None
-        out = None
-        for blk in layers:
-            for cls, K, N, epi, src, wq, ws, b, a in blk:
-                if epi == "gelu_requant":
-                    _, hq, hs = ops.gemm(a[0], a[1], wq, ws, b, gelu=True, requant=True, write_d=False)
-                    hidden = (hq, hs)
-                elif src.startswith("ffn"):
-                    out = ops.gemm(hidden[0], hidden[1], wq, ws, b)
-                else:
-                    out = ops.gemm(a[0], a[1], wq, ws, b)
-        return out
-
-    flops = 0.0
-    for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
-        flops += 2.0 * toks[cls] * K * N
-    flops *= blocks
-    desc = (f"DiT linear stack (BASELINE config 3): {blocks} blocks x 28 FP8 GEMMs, CFG batch 2, tokens per rank "
-            f"video {toks['video']} / audio {toks['audio']} / text {toks['text']} ({scaling} scaling)")
-    # kernels per step: each GEMM's launches (split-K GEMM and reduction where the shape splits)
-    launches = 0
-    for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
-        launches += ops.gemm_plan(toks[cls], N, K, dev)["launches"]
-    launches *= blocks
-    return step, flops, launches, desc, toks
-
-
-# ----------------------------------------------------------------------------- CPU baseline (oracle port)
-def cpu_reference_sample(name: str, rows: int, seed: int = 0):
-    """The reference's CPU path on `rows` tokens of the workload, restated by the oracle:
-    quantise x (1x128), dequantise, fp32 matmul with the dequantised weight, + bias, bf16;
-    for the FFN the bf16 GELU and the requantisation of the hidden state in between.
-    Returns (seconds per sample, flops per sample, threads)."""
-    import numpy as np
-    from oracle import oracle as O
-
-    rng = np.random.default_rng(seed)
-    desc, _, layers = WORKLOADS[name]
-    K0 = layers[0][0]
-    x = rng.standard_normal((rows, K0), dtype=np.float32)
-    x[:, rng.permutation(K0)[: max(1, K0 // 100)]] *= 20.0
-    xb = O.f32_to_bf16(x)
-    mats = []
-    for K, N, epi in layers:
-        w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
-        wq, ws = O.quant_weight_128x128(w)
-        wd = O.dequant_weight_f32(wq, ws)          # load-time, untimed
-        b = O.bf16_to_f32(O.f32_to_bf16(rng.standard_normal(N, dtype=np.float32) * 0.01))
-        lora = None
-        if epi.startswith("lora"):
-            r = int(epi[4:])
-            lora = (O.bf16_to_f32(O.f32_to_bf16(rng.standard_normal((r, K), dtype=np.float32) * 0.01)),
-                    O.bf16_to_f32(O.f32_to_bf16(rng.standard_normal((N, r), dtype=np.float32) * 0.01)))
-        mats.append((K, N, epi, wd, b, lora))
-
-    def run():
-        cur = xb
-        for K, N, epi, wd, b, lora in mats:
-            q, s = O.quant_act_1x128(cur)
-            a = O.dequant_act_f32(q, s)
-            d = a @ wd.T + b[None, :]
-            if lora is not None:
-                d = d + (O.bf16_to_f32(cur) @ lora[0].T) @ lora[1].T
-            h = O.f32_to_bf16(d)
-            if epi == "gelu_requant":
-                h = O.gelu_tanh_bf16(h)
-            cur = h
-        return cur
-
-    run()  # warm
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        run()
-        reps += 1
-        el = time.perf_counter() - t0
-        if el > 8.0 or reps >= 50:
-            break
-    threads = os.cpu_count() or 1
-    try:
-        from threadpoolctl import threadpool_info
-        info = [i for i in threadpool_info() if i.get("user_api") == "blas"]
-        if info:
-            threads = max(int(i.get("num_threads", 1)) for i in info)
-    except Exception:  # noqa: BLE001
-        pass
-    return el / reps, flops_of(name, rows), threads
-
-
-
-def cpu_dit_sample(toks: dict, seed: int = 0):
-    """One block of the config-3 stack on a few tokens per class through the oracle's
-    restatement of the reference CPU path.  Returns (seconds, flops, threads)."""
-    import numpy as np
-    from oracle import oracle as O
-
-    rng = np.random.default_rng(seed)
-    acts = {}
-    for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
-        if (cls, K) not in acts and not src.startswith("ffn"):
-            x = rng.standard_normal((toks[cls], K), dtype=np.float32)
-            acts[(cls, K)] = O.f32_to_bf16(x)
-    mats = []
-    for cls, K, N, epi, src in DIT_BLOCK_GEMMS:
-        wq, ws = O.quant_weight_128x128(rng.standard_normal((N, K), dtype=np.float32) * 0.02)
-        mats.append((cls, K, N, epi, src, O.dequant_weight_f32(wq, ws)))
-
-    def run():
-        hidden = None
-        for cls, K, N, epi, src, wd in mats:
-            inp = hidden if src.startswith("ffn") else acts[(cls, K)]
-            q, sc = O.quant_act_1x128(inp)
-            h = O.f32_to_bf16(O.dequant_act_f32(q, sc) @ wd.T)
-            if epi == "gelu_requant":
-                hidden = O.gelu_tanh_bf16(h)
-
-    run()
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        run()
-        reps += 1
-        el = time.perf_counter() - t0
-        if el > 8.0 or reps >= 20:
-            break
-    flops = sum(2.0 * toks[c] * K * N for c, K, N, _, _ in DIT_BLOCK_GEMMS)
-    return el / reps, flops, os.cpu_count() or 1
-
-
-def run_dit(args, rank: int, world: int, local: int):
-    """Config 3: the DiT linear stack, token-sharded over the ranks (strong scaling by default)."""
-    scaling = args.scaling or "strong"
-    sample = {"video": 512, "audio": 64, "text": 64}
+def run_single(args, rank: int, world: int, local: int):
+    desc, M_default, layers = WORKLOADS[args.workload]
+    M = args.m or M_default
+    rows = 512 if args.workload != "linear" else 1024
     if args.impl == "reference":
         if rank != 0:
             return
-        per, fl, threads = cpu_dit_sample(sample)
+        per, fl, threads, kind = cpu_reference_layers(single_cpu_layers(args.workload), rows)
         val = fl / per / 1e12
         print(json.dumps({
-            "metric": "blockwise-FP8 dit_step TFLOP/s", "value": val, "unit": "TFLOP/s", "impl": "reference",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
-            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "DiT linear stack (BASELINE config 3), one block sampled", "sample_tokens": sample},
-            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                             "sample": f"one of {args.blocks} blocks, tokens {sample}; oracle restatement of the "
-                                       "reference CPU path"},
+            "metric": f"blockwise-FP8 {args.workload} TFLOP/s", "value": val, "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": flops_of(args.workload, M) / (val * 1e12) * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantised e4m3 operands)", "data": "synthetic",
+            "config": {"workload": desc, "tokens_per_gpu": M},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                             "sample": f"{rows} of {M} tokens per step, same layers; the reference's CPU torch "
+                                       "path (runtime LoRA not included)"},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
 
@@ -478,9 +879,11 @@ def run_dit(args, rank: int, world: int, local: int):
     torch.cuda.set_device(dev)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
-    step, flops, launches, desc, toks = build_dit_step(dev, world, rank, scaling, args.blocks)
+    x, params = build_workload(args.workload, M, dev, seed=1234 + rank)
+    step, n_ev = make_step(x, params)
+    names = kernel_names(args.workload)
 
     def barrier():
         if world > 1:
@@ -491,50 +894,43 @@ def run_dit(args, rank: int, world: int, local: int):
         step()
     barrier()
     assert ops.device_status() == 0
-    # The step is 1344 launches; at several GPUs most of them are shorter than
-    # the host's per-call overhead, so the whole step is captured once as a CUDA
-    # graph (the C ABI neither allocates nor synchronises) and replayed.
-    graph = None
-    if not args.no_graph:
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            step()
-        torch.cuda.current_stream(dev).wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        for _ in range(2):
-            graph.replay()
-        barrier()
-    run_step = graph.replay if graph is not None else step
-    clocks = ClockSampler(local)
-    clocks.start()
-    barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        run_step()
-    t1.record()
-    barrier()
-    elapsed = t0.elapsed_time(t1)
 
-    # End to end: this rank's bf16 token streams come from pinned host memory, are
-    # quantised (public ops API), run through the stack, and the last output returns.
-    hosts = {c: torch.randn(toks[c], 4096 if c != "audio" else 2048).to(torch.bfloat16).pin_memory()
-             for c in toks}
-    out_host = torch.empty((toks["audio"], 2048), dtype=torch.bfloat16).pin_memory()
+    clocks = ClockSampler(local).start()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
+    barrier()
+    t_start, t_end = _events()
+    t_start.record()
+    for i in range(args.steps):
+        step(evs[i])
+    t_end.record()
+    barrier()
+    elapsed = t_start.elapsed_time(t_end)
+    per_kernel = [0.0] * (n_ev - 1)
+    for i in range(args.steps):
+        for j in range(n_ev - 1):
+            per_kernel[j] += evs[i][j].elapsed_time(evs[i][j + 1])
+    per_kernel = [t / args.steps for t in per_kernel]
+
+    # End to end through the public layer modules over pinned host tokens, streamed in
+    # token chunks (ltx_kernels.blockwise.host_stream); --e2e-chunk 0: one whole-batch
+    # copy in, the layer, one copy out.
+    from ltx_kernels.blockwise.host_stream import TokenStreamer
+    x_host = x.cpu().pin_memory()
+    out_dim = params[-1][1]
+    out_host = torch.empty((M, out_dim), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+    layer = build_module(args.workload, params, dev)
+    chunk = args.e2e_chunk if args.e2e_chunk > 0 else M
+    streamer = TokenStreamer(layer, x.shape[1], chunk, dev)
 
     def e2e_step():
-        for c, h in hosts.items():
-            ops.quantize_1x128(h.to(dev, non_blocking=True))
-        out = step()
-        out_host.copy_(out, non_blocking=True)
+        with torch.inference_mode():
+            streamer(x_host, out_host)
 
-    e2e_step()
+    for _ in range(2):
+        e2e_step()
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(1, min(args.steps, 3))
+    e0, e1 = _events()
     e0.record()
     for _ in range(e2e_steps):
         e2e_step()
@@ -547,45 +943,120 @@ def run_dit(args, rank: int, world: int, local: int):
         t = torch.tensor([elapsed, e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed, e2e_ms = t.tolist()
-    ms = elapsed / args.steps
-    total_flops = flops * (world if scaling == "weak" else 1)
-    if scaling == "strong":
-        total_flops = sum(2.0 * DIT_TOKENS[c] * K * N for c, K, N, _, _ in DIT_BLOCK_GEMMS) * args.blocks
-    value = total_flops / (ms * 1e-3) / 1e12
-    peak = measure_fp8_peak(dev) if rank == 0 else None
+
+    fl = flops_of(args.workload, M)
+    ms_per_step = elapsed / args.steps
+    gemm_idx = [j for j, n in enumerate(names) if n.startswith("gemm")]
+    dom = max(gemm_idx, key=lambda j: per_kernel[j])
+    K, N, epi = layers[gemm_idx.index(dom)]
+    dom_flops = 2.0 * M * N * K + (2.0 * M * int(epi[4:]) * N if epi.startswith("lora") else 0.0)
+    achieved = dom_flops / (per_kernel[dom] * 1e-3) / 1e12
+    pk, pk_src = fp8_peak()
+    traffic = None
+    try:
+        with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
+            tr = json.load(f).get(f"{args.workload}:{names[dom]}")
+        traffic = tr["bytes_per_launch_at_bench_size"] if tr else None
+    except (OSError, ValueError, KeyError):
+        traffic = None
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            per, fl, threads = cpu_dit_sample(sample)
-            cpu = {"value": fl / per / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                   "sample": f"one block, tokens {sample}; oracle restatement of the reference CPU path"}
-        h2d = sum(h.numel() * 2 for h in hosts.values())
+            per, flc, threads, kind = cpu_reference_layers(single_cpu_layers(args.workload), rows)
+            cpu = {"value": flc / per / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                   "sample": f"{rows} of {M} tokens, same layers, the reference's CPU torch path"}
         print(json.dumps({
-            "metric": "blockwise-FP8 dit_step TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out",
+            "metric": f"blockwise-FP8 {args.workload} TFLOP/s",
+            "value": world * fl / (ms_per_step * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out",
             "data": "synthetic (seeded; BASELINE.json distributions)",
-            "config": {"workload": desc, "tokens_per_rank": toks, "blocks": args.blocks,
-                       "parallelism": f"token-sharded over {world} GPU(s), weights replicated, no collective",
-                       "l2": "per-block weights 385 MB > L2; no flush"},
-            "roofline": {"bound": "tensor", "kernel": "fp8_blockwise_gemm_kernel (all 28 shapes)",
-                         "achieved": flops / (ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
-                         "frac": (flops / (ms * 1e-3) / 1e12 / peak) if peak else None,
-                         "peak_source": "cuBLASLt e4m3 GEMM (torch._scaled_mm 8192^3, burst) measured in this run",
-                         "traffic": None},
+            "config": {"workload": desc, "tokens_per_gpu": M, "layers": [list(l) for l in layers],
+                       "parallelism": f"token-sharded dp{world}, weights replicated",
+                       "l2": "working set > L2 (x 201 MB + weights + 403 MB fp8 hidden state); no flush"},
+            "kernels_ms": {n: round(t, 4) for n, t in zip(names, per_kernel)},
+            "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": pk,
+                         "unit": "TFLOP/s", "frac": achieved / pk, "peak_source": pk_src,
+                         "frac_of_nominal_4500": achieved / NOMINAL_FP8_TFLOPS, "traffic": traffic},
             "cpu_baseline": cpu,
-            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_host.numel() * 2},
-            "gpu_launches": args.steps * launches,
-            "cuda_graph": graph is not None,
+            "e2e": {"value": world * fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": M * out_dim * 2,
+                    "api": f"{type(layer).__name__} via host_stream.TokenStreamer, {chunk}-token chunks"},
+            "gpu_launches": args.steps * ((n_ev - 1) + sum(ops.gemm_plan(M, N, K, dev)["launches"] - 1
+                                                           for K, N, _ in layers)),
             "clocks": clk,
         }))
-    del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
-# ----------------------------------------------------------------------------- main
+
+# ----------------------------------------------------------------------------- config-4 sweep
+SWEEP_M = (128, 512, 2048, 8192, 32768, 65536)
+SWEEP_KN = ((2048, 2048), (4096, 4096), (4096, 16384), (16384, 4096))
+
+
+def run_sweep(args, rank: int, world: int, local: int):
+    """M x (K, N) GEMMs (bias, bf16 out), each event-timed in isolation
+    (L2 flushed between launches when the working set fits in L2), reported against the
+    bound that applies at its arithmetic intensity (HBM GB/s or FP8 TFLOP/s), with the
+    reference's SM89 GEMM on the same inputs beside it."""
+    import torch
+    from ltx_kernels.blockwise import ops
+    from oracle import refpath
+    if args.impl == "reference" or rank != 0:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the sweep is a GPU roofline map; the reference's "
+                              "CPU path is timed by the other workloads"}))
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    G = refpath.gemm() if refpath.available("gemm") else None
+    pk, pk_src = fp8_peak()
+    bw, bw_src = hbm_peak()
+    ridge = pk * 1e12 / (bw * 1e9)
+    flush = L2Flush(dev)
+    g = torch.Generator(device=dev).manual_seed(9)
+    points, tot_fl, tot_ms = [], 0.0, 0.0
+    clk = ClockSampler(local).start()
+    for K, N in SWEEP_KN:
+        wq, ws, b = synth_weight(N, K, g, dev)
+        for M in SWEEP_M:
+            aq, asc = ops.quantize_1x128(synth_acts(M, K, g, dev))
+            small = M * K + N * K + 2 * M * N < (126 << 20)
+            f = lambda: ops.gemm(aq, asc, wq, ws, b)
+            ms = time_launches(f, 20 if M <= 2048 else 8, flush=flush if small else None)
+            fl, by = 2.0 * M * N * K, gemm_alg_bytes(M, K, N, "bias")
+            ai = fl / by
+            bound = "hbm" if ai < ridge else "tensor"
+            p = {"M": M, "K": K, "N": N, "ms": ms, "tflops": fl / ms / 1e9, "gbs": by / ms / 1e6,
+                 "alg_bytes": by, "intensity": ai, "bound": bound, "launches": ops.gemm_plan(M, N, K, dev)["launches"],
+                 "frac": (by / ms / 1e6) / bw if bound == "hbm" else (fl / ms / 1e9) / pk,
+                 "l2": "flushed" if small else "working set > L2"}
+            if G is not None:
+                def ref():
+                    d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                    G.fp8_gemm_nt_sm89((aq, asc), (wq, ws), d, b, use_fast_accum=False)
+                rms = time_launches(ref, 5 if M <= 2048 else 3, warmup=1, flush=flush if small else None)
+                p["ref_sm89_ms"], p["speedup_vs_sm89"] = rms, rms / ms
+            points.append(p)
+            tot_fl += fl
+            tot_ms += ms
+            del aq, asc
+        del wq, ws
+    c = clk.stop()
+    print(json.dumps({
+        "metric": "blockwise-FP8 GEMM sweep (BASELINE config 4) TFLOP/s", "value": tot_fl / tot_ms / 1e9,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": 1, "warmup": 3, "ms_per_step": tot_ms, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out",
+        "data": "synthetic (seeded; BASELINE.json distributions)",
+        "config": {"workload": "config-4 roofline sweep", "M": list(SWEEP_M), "KN": [list(k) for k in SWEEP_KN]},
+        "peaks": {"fp8_tflops": pk, "fp8_source": pk_src, "hbm_gbs": bw, "hbm_source": bw_src,
+                  "ridge_flop_per_byte": ridge},
+        "points": points, "e2e": None, "cpu_baseline": None, "gpu_launches": sum(p["launches"] for p in points) * 8,
+        "clocks": c}))
+
+
 # ----------------------------------------------------------------------------- producers
 PROD_B, PROD_S, PROD_H, PROD_HEADS = 2, 24576, 4096, 32   # config 3 video tokens (CFG batch 2), d = 4096
 
@@ -782,9 +1253,10 @@ def run_producers(args, rank: int, world: int, local: int):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ffn", choices=sorted(WORKLOADS) + ["dit_step", "producers"])
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="dit_step",
+                    choices=["dit_step"] + sorted(WORKLOADS) + ["producers", "sweep"])
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="dit_step: strong (default) splits one step's tokens over the ranks, weak gives every "
                          "rank a full step")
@@ -792,6 +1264,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--m", type=int, default=0, help="tokens per GPU (default: the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="dit_step: skip the headline-GEMM, GPU-reference and cuBLAS measurements")
     ap.add_argument("--e2e-chunk", type=int, default=2048,
                     help="ffn/linear/qkv_lora e2e: tokens per streamed chunk (0: whole batch, copies not overlapped)")
     ap.add_argument("--no-graph", action="store_true", help="dit_step: launch every GEMM from Python instead of "
@@ -806,165 +1280,9 @@ def main():
         return run_dit(args, rank, world, local)
     if args.workload == "producers":
         return run_producers(args, rank, world, local)
-    desc, M_default, layers = WORKLOADS[args.workload]
-    M = args.m or M_default
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        rows = 512 if args.workload != "linear" else 1024
-        per, fl, threads = cpu_reference_sample(args.workload, rows)
-        val = fl / per / 1e12
-        out = {"metric": f"blockwise-FP8 {args.workload} TFLOP/s", "value": val, "unit": "TFLOP/s",
-               "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-               "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-               "dtype": "f32", "data": "synthetic",
-               "config": {"workload": desc, "tokens_per_gpu": M, "sample_tokens": rows},
-               "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                                "sample": f"{rows} of {M} tokens per step, same layers; oracle restatement of "
-                                          "the reference CPU path (dequantise + fp32 matmul)"},
-               "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(out))
-        return
-
-    import torch
-    import torch.distributed as dist
-    from ltx_kernels.blockwise import ops
-
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-
-    x, params = build_workload(args.workload, M, dev, seed=1234 + rank)
-    step, n_ev = make_step(x, params)
-    names = kernel_names(args.workload)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    assert ops.device_status() == 0
-
-    clocks = ClockSampler(local)
-    clocks.start()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
-    barrier()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record()
-    for i in range(args.steps):
-        step(evs[i])
-    t_end.record()
-    barrier()
-    elapsed = t_start.elapsed_time(t_end)
-    per_kernel = [0.0] * (n_ev - 1)
-    for i in range(args.steps):
-        for j in range(n_ev - 1):
-            per_kernel[j] += evs[i][j].elapsed_time(evs[i][j + 1])
-    per_kernel = [t / args.steps for t in per_kernel]
-
-    # ---- end to end through the public API with host buffers: the layer modules
-    # (BlockwiseFP8FeedForward / BlockwiseFP8Linear / BlockwiseFP8LoRALinear) over
-    # pinned host tokens, H2D and D2H inside the timed region, streamed in token
-    # chunks so the copies of neighbouring chunks overlap the GEMMs
-    # (ltx_kernels.blockwise.host_stream); --e2e-chunk 0 copies the whole batch in,
-    # runs the layer and copies it out, one after the other.
-    from ltx_kernels.blockwise.host_stream import TokenStreamer
-    x_host = x.cpu().pin_memory()
-    out_dim = params[-1][1]
-    out_host = torch.empty((M, out_dim), dtype=torch.bfloat16).pin_memory()
-    e2e_steps = max(3, min(args.steps, 10))
-    layer = build_module(args.workload, params, dev)
-    chunk = args.e2e_chunk if args.e2e_chunk > 0 else M
-    streamer = TokenStreamer(layer, x.shape[1], chunk, dev)
-
-    def e2e_step():
-        with torch.inference_mode():
-            streamer(x_host, out_host)
-
-    for _ in range(2):
-        e2e_step()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    clk = clocks.stop()
-    assert ops.device_status() == 0
-
-    if world > 1:
-        t = torch.tensor([elapsed, e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, e2e_ms = t.tolist()
-
-    fl = flops_of(args.workload, M)
-    ms_per_step = elapsed / args.steps
-    value = world * fl / (ms_per_step * 1e-3) / 1e12
-    e2e_value = world * fl / (e2e_ms * 1e-3) / 1e12
-
-    # ---- roofline of the dominant kernel (largest share of the step)
-    gemm_idx = [j for j, n in enumerate(names) if n.startswith("gemm")]
-    dom = max(gemm_idx, key=lambda j: per_kernel[j])
-    lay = [l for l in layers]
-    li = gemm_idx.index(dom)
-    K, N, epi = lay[li]
-    dom_flops = 2.0 * M * N * K + (2.0 * M * int(epi[4:]) * N if epi.startswith("lora") else 0.0)
-    achieved = dom_flops / (per_kernel[dom] * 1e-3) / 1e12
-    peak = measure_fp8_peak(dev) if rank == 0 else None
-    traffic = None
-    tpath = os.path.join(REPO, "profiles", "ncu_traffic.json")
-    if os.path.exists(tpath):
-        try:
-            tr = json.load(open(tpath)).get(f"{args.workload}:{names[dom]}")
-            if tr:
-                traffic = tr["bytes_per_launch_at_bench_size"]
-        except (ValueError, KeyError):
-            traffic = None
-
-    if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline and world == 1:
-            rows = 512 if args.workload != "linear" else 1024
-            per, flc, threads = cpu_reference_sample(args.workload, rows)
-            cpu = {"value": flc / per / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                   "sample": f"{rows} of {M} tokens, same layers, oracle restatement of the reference's CPU path "
-                             "(1x128 quant, dequantise, fp32 numpy matmul, bias, bf16; GELU+requant for the FFN)"}
-        out = {
-            "metric": f"blockwise-FP8 {args.workload} TFLOP/s",
-            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out", "data": "synthetic (seeded; BASELINE.json distributions)",
-            "config": {"workload": desc, "tokens_per_gpu": M, "layers": [list(l) for l in layers],
-                       "parallelism": f"token-sharded dp{world}, weights replicated",
-                       "l2": "working set > L2 (x 201 MB + weights + 403 MB fp8 hidden state); no flush"},
-            "kernels_ms": {n: round(t, 4) for n, t in zip(names, per_kernel)},
-            "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s",
-                         "frac": (achieved / peak) if peak else None,
-                         "peak_source": "cuBLASLt e4m3 GEMM (torch._scaled_mm 8192^3, burst) measured in this run",
-                         "frac_of_nominal_4500": achieved / NOMINAL_FP8_TFLOPS,
-                         "traffic": traffic},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": M * out_dim * 2,
-                    "api": f"{type(layer).__name__} via host_stream.TokenStreamer, {chunk}-token chunks"},
-            "gpu_launches": args.steps * ((n_ev - 1) + sum(ops.gemm_plan(M, N, K, dev)["launches"] - 1
-                                                           for K, N, _ in layers)),
-            "clocks": clk,
-        }
-        print(json.dumps(out))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    if args.workload == "sweep":
+        return run_sweep(args, rank, world, local)
+    return run_single(args, rank, world, local)
 
 
 if __name__ == "__main__":

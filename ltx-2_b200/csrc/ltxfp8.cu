@@ -146,6 +146,10 @@ int gemm_launch(DeviceInfo* d, const CUtensorMap& a, const CUtensorMap& b, const
   int rc = gemm_prepare<kGelu, kRequant>(d);
   if (rc) return rc;
   const int units = p.total_tiles * p.k_splits;
+  // Split-K units write their partials through the pipeline stages' shared
+  // memory, which is only idle if every CTA runs exactly one unit.
+  if (p.k_splits > 1 && units > d->sms)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gemm: split-K launch of %d units exceeds the %d SMs", units, d->sms);
   const int grid = units < d->sms ? units : d->sms;
   fp8_blockwise_gemm_kernel<kGelu, kRequant><<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(a, b, lx, lb, md, mq, p);
   cudaError_t e = cudaGetLastError();

@@ -6,14 +6,38 @@ place like the pybind function it replaces, so the reference's own
 ``linear.py`` (``from blockwise_cpp import fp8_gemm_nt_sm89``, linear.py:30)
 runs on the tcgen05 kernel without edits.  ``use_fast_accum`` is ignored:
 accumulation is always fp32.
+
+This directory (``ltx-2_b200/dropin``) holds only this module, so putting it
+first on ``sys.path`` replaces the compiled GEMM and nothing else: the name
+``ltx_kernels`` keeps resolving to the reference's package.  The C-ABI binding
+(``ltx_kernels/_lib.py``, ``ltx_kernels/blockwise/ops.py`` of this repository) is
+therefore loaded from its files under the private package name ``_ltxb200``.
 """
 from __future__ import annotations
 
+import importlib
+import os
+import sys
+import types
 from typing import Optional, Sequence
 
 import torch
 
-from ltx_kernels.blockwise import ops
+_KERNELS = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "ltx_kernels")
+
+
+def _load_ops():
+    if "_ltxb200.blockwise.ops" not in sys.modules:
+        for name, path in (("_ltxb200", _KERNELS), ("_ltxb200.blockwise", os.path.join(_KERNELS, "blockwise"))):
+            if name not in sys.modules:
+                pkg = types.ModuleType(name)
+                pkg.__path__ = [path]  # package without running its __init__ (which imports by the public name)
+                sys.modules[name] = pkg
+    return importlib.import_module("_ltxb200.blockwise.ops")
+
+
+ops = _load_ops()
 
 
 def fp8_gemm_nt_sm89(a: Sequence[torch.Tensor], b: Sequence[torch.Tensor], d: torch.Tensor,

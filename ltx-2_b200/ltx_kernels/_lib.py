@@ -148,5 +148,6 @@ GEMM_CTA_PAIR = 2
 def set_gemm_variant(variant: int) -> None:
     """Force the GEMM kernel (GEMM_AUTO, GEMM_ONE_CTA, GEMM_CTA_PAIR); process-wide."""
     check(load().ltxfp8_gemm_set_variant(variant))
-    from .blockwise import ops  # the split-K workspace size depends on the kernel
+    from .blockwise import ops  # the split-K workspace size and the launch plan depend on the kernel
     ops._WS_CACHE.clear()
+    ops._PLAN_CACHE.clear()

@@ -145,15 +145,15 @@ def _rms_fma_fake(x, y, z):
 @torch.library.custom_op("blockwise::gated_attention", mutates_args=())
 def _gated_attention(x: torch.Tensor, gate_logits: torch.Tensor, quantize: bool = True
                      ) -> Tuple[torch.Tensor, torch.Tensor]:
-    """x * 2 sigmoid(gate_logits) per head, then 1x128 e4m3 (triton_ops.py:309-345).
-    With quantize=False the bf16 output comes with an empty scale tensor (a custom op
-    cannot return None; ``gated_attention_triton`` turns it into None like the reference)."""
+    """x * 2 sigmoid(gate_logits) per head, then 1x128 e4m3 (triton_ops.py:309-384).
+    With quantize=False the bf16 output comes with None in place of the scales, as the
+    reference's op returns (triton_ops.py:367-370, 384)."""
     b, t, h = x.shape
     if quantize:
         q, sc = ops.gated_attention(x, gate_logits, True, _QUANT_MODE)
         return q.view(b, t, h), sc
     out = ops.gated_attention(x, gate_logits, False, _QUANT_MODE)
-    return out.view(b, t, h), torch.empty(0, dtype=torch.float32, device=x.device)
+    return out.view(b, t, h), None
 
 
 @_gated_attention.register_fake
@@ -161,7 +161,7 @@ def _gated_attention_fake(x, gate_logits, quantize=True):
     b, t, h = x.shape
     if quantize:
         return (torch.empty((b, t, h), dtype=torch.float8_e4m3fn, device=x.device), _scales_like(b * t, h, x.device))
-    return torch.empty((b, t, h), dtype=torch.bfloat16, device=x.device), torch.empty(0, device=x.device)
+    return torch.empty((b, t, h), dtype=torch.bfloat16, device=x.device), None
 
 
 def blockwise_quantize_adanorm_triton(x: torch.Tensor, w: Optional[torch.Tensor], norm_scale: torch.Tensor,
@@ -184,8 +184,7 @@ def rms_fma_triton(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor) -> torch.T
 
 def gated_attention_triton(x: torch.Tensor, gate_logits: torch.Tensor, quantize: bool = True):
     """triton_ops.py:444 (``run_gated_attention``): (e4m3, scales), or (bf16, None)."""
-    out, sc = _gated_attention(x, gate_logits, quantize)
-    return (out, sc) if quantize else (out, None)
+    return _gated_attention(x, gate_logits, quantize)
 
 
 # ----------------------------------------------------------------------------- RMSNorm + RoPE

@@ -340,15 +340,36 @@ def lora_exact_f32(x_bf16_rows: np.ndarray, lora_a_bf16: np.ndarray, lora_b_bf16
 
 
 # ----------------------------------------------------------------------------- metrics
-def error_metrics(out: np.ndarray, ref: np.ndarray) -> dict:
-    """Relative Frobenius error, max-abs error and max-abs error normalised by max|ref|."""
+def bf16_ulp(a: np.ndarray) -> np.ndarray:
+    """Spacing of bf16 values at |a| (8 significant bits): 2^(floor(log2|a|) - 7), 0 at 0."""
+    a = np.abs(np.asarray(a, np.float64))
+    _, e = np.frexp(a)  # a = m 2^e, m in [0.5, 1)
+    ulp = np.ldexp(1.0, np.maximum(e - 8, -133))
+    return np.where(a == 0, 0.0, ulp)
+
+
+def error_metrics(out: np.ndarray, ref: np.ndarray, abs_tol: float = 2e-2) -> dict:
+    """Error of a bf16 result against an fp32/fp64 reference.
+
+    * ``rel_fro``       -- ||out - ref||_F / ||ref||_F.
+    * ``max_abs``       -- max |out - ref| (raw).
+    * ``max_abs_norm``  -- max |out - ref| / max |ref| (informative).
+    * ``bound_excess``  -- max over elements of |out - ref| - (abs_tol + ulp_bf16(|ref|)):
+      <= 0 means every element is within ``abs_tol`` absolute plus one bf16 ulp of the
+      reference, which a correctly rounded bf16 result always meets (its rounding
+      error is at most half an ulp), however large the element.
+    * ``frac_over_abs`` -- fraction of elements with |out - ref| > abs_tol.
+    """
     o = out.astype(np.float64)
     r = ref.astype(np.float64)
-    diff = o - r
-    fro = float(np.linalg.norm(diff) / max(np.linalg.norm(r), 1e-30))
-    mx = float(np.max(np.abs(diff))) if diff.size else 0.0
+    diff = np.abs(o - r)
+    fro = float(np.linalg.norm(o - r) / max(np.linalg.norm(r), 1e-30))
+    mx = float(np.max(diff)) if diff.size else 0.0
     scale = float(np.max(np.abs(r))) if r.size else 1.0
-    return {"rel_fro": fro, "max_abs": mx, "max_abs_norm": mx / max(scale, 1e-30)}
+    excess = float(np.max(diff - (abs_tol + bf16_ulp(r)))) if diff.size else -abs_tol
+    over = float(np.mean(diff > abs_tol)) if diff.size else 0.0
+    return {"rel_fro": fro, "max_abs": mx, "max_abs_norm": mx / max(scale, 1e-30), "bound_excess": excess,
+            "frac_over_abs": over}
 
 
 def codes_equal(a: np.ndarray, b: np.ndarray) -> np.ndarray:

@@ -9,7 +9,8 @@ import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(REPO, "ltx-2_b200")
-for p in (PKG, REPO):
+DROPIN = os.path.join(PKG, "dropin")  # blockwise_cpp, the reference's compiled-module name
+for p in (DROPIN, PKG, REPO):
     if p not in sys.path:
         sys.path.insert(0, p)
 

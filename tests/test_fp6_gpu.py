@@ -56,4 +56,4 @@ def test_fp6_weight_quant_and_linear(cuda_device):
     torch.cuda.synchronize()
     ref = O.gemm_dequant_f32(bits(aq), scales_mn(asc, M), bits(q), s.cpu().numpy(), lin.bias.detach().float().cpu().numpy())
     m = O.error_metrics(O.bf16_to_f32(bits(y.view(M, N))), ref)
-    assert m["rel_fro"] <= 1e-2 and m["max_abs_norm"] <= 2e-2, m
+    assert m["rel_fro"] <= 1e-2 and m["bound_excess"] <= 0, m  # |d - ref| <= 2e-2 + 1 bf16 ulp

@@ -1,10 +1,10 @@
 """GPU parity of the tcgen05 blockwise GEMM and its fused epilogues against the oracle.
 
-Tolerance (from the task's parity bar): relative Frobenius error <= 1e-2 and
-max-abs error <= 2e-2 of the reference's dequantise-then-fp32-matmul result.
-The max-abs bound is applied normalised by max|reference|: one bf16 ulp of the
-output is already 0.0625 at |D| in [8, 16), so an absolute 2e-2 would fail on
-rounding of a correct result.  The kernel is in fact ~1e-3 (bf16 output rounding).
+Tolerance (the parity bar): relative Frobenius error <= 1e-2 and, element by
+element, |D - ref| <= 2e-2 + one bf16 ulp of |ref| against the reference's
+dequantise-then-fp32-matmul result.  The ulp term is what a correctly rounded
+bf16 output needs (one ulp is already 0.0625 at |D| in [8, 16)); it does not grow
+with max|ref| the way a normalised bound would.
 """
 from __future__ import annotations
 
@@ -18,7 +18,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 REL_FRO = 1e-2
-MAX_ABS_NORM = 2e-2
+ABS_TOL = 2e-2
 
 
 def _problem(M, N, K, dev, seed=0, with_bias=True):
@@ -38,9 +38,9 @@ def _oracle(aq, asc, wq, wsc, b, rows=None):
 
 
 def _check(out_bf16, ref_f32):
-    m = O.error_metrics(O.bf16_to_f32(bits(out_bf16)), ref_f32)
+    m = O.error_metrics(O.bf16_to_f32(bits(out_bf16)), ref_f32, abs_tol=ABS_TOL)
     assert np.isfinite(O.bf16_to_f32(bits(out_bf16))).all()
-    assert m["rel_fro"] <= REL_FRO and m["max_abs_norm"] <= MAX_ABS_NORM, m
+    assert m["rel_fro"] <= REL_FRO and m["bound_excess"] <= 0, m
     return m
 
 
@@ -369,10 +369,10 @@ def test_tail_wave_split(cuda_device, M, N, K):
     rows = np.unique(np.concatenate([np.arange(0, M, max(1, M // 40)), [r0 - 1, r0, r0 + 1, M - 1]]))
     ri = torch.from_numpy(rows).to(cuda_device)
     ref = O.gemm_dequant_f32(bits(aq[ri]), scales_mn(asc, M)[:, rows], bits(wq), wsc.cpu().numpy(), b.cpu().numpy())
-    m = O.error_metrics(O.bf16_to_f32(bits(d[ri])), ref)
-    assert m["rel_fro"] <= REL_FRO and m["max_abs_norm"] <= MAX_ABS_NORM, m
-    diff = (d.float() - d1.float()).abs().max().item()
-    assert diff <= 0.02 * d1.float().abs().max().item()
+    m = O.error_metrics(O.bf16_to_f32(bits(d[ri])), ref, abs_tol=ABS_TOL)
+    assert m["rel_fro"] <= REL_FRO and m["bound_excess"] <= 0, m
+    m1 = O.error_metrics(O.bf16_to_f32(bits(d)), O.bf16_to_f32(bits(d1)), abs_tol=ABS_TOL)
+    assert m1["bound_excess"] <= 0, m1
     assert torch.equal(d[:r0], d1[:r0])  # the unsplit rows run the same kernel over the same K order
     assert torch.equal(d, ops.gemm(aq, asc, wq, wsc, b))
     # fused GELU + requant through the split rows' reduction

@@ -79,8 +79,8 @@ def test_fuse_rule_and_merged_gemm(cuda_device):
     torch.cuda.synchronize()
     ref_merged = O.gemm_dequant_f32(bits(aq), scales_mn(asc, M), bits(q2), s2.cpu().numpy(), None)
     m = O.error_metrics(O.bf16_to_f32(bits(d_merged)), ref_merged)
-    assert m["rel_fro"] <= 1e-2 and m["max_abs_norm"] <= 2e-2, m
+    assert m["rel_fro"] <= 1e-2 and m["bound_excess"] <= 0, m  # |d - ref| <= 2e-2 + 1 bf16 ulp
     ref_exact = O.gemm_dequant_f32(bits(aq), scales_mn(asc, M), bits(wq), wsc.cpu().numpy(), None) \
         + O.lora_exact_f32(bits(x), bits(a), bits(b), strength)
     m = O.error_metrics(O.bf16_to_f32(bits(d_runtime)), ref_exact)
-    assert m["rel_fro"] <= 1e-2 and m["max_abs_norm"] <= 2e-2, m
+    assert m["rel_fro"] <= 1e-2 and m["bound_excess"] <= 0, m  # |d - ref| <= 2e-2 + 1 bf16 ulp

@@ -1,0 +1,363 @@
+"""The product against the reference's own B200 path, on the same inputs (needs oracle/_ref).
+
+On Blackwell the reference runs the Triton 1x128 quantiser (``triton_ops.py:102-151``)
+and the SM89 ``mma.sync`` GEMM with fp32 accumulation (``linear.py:25-35,98-104``,
+``csrc/blockwise/kernels/geforce/gemm.cu``); its producers are the Triton kernels of
+``triton_ops.py:52-384`` and its q/k RMSNorm + RoPE the ``ops_cpp`` CUDA kernels.
+``oracle/build_ref.py`` builds those from the reference checkout into ``oracle/_ref``
+and ``oracle/refpath.py`` loads them next to this package.
+
+Bars:
+* quantiser: codes and scales bit-exact with the reference's Triton kernel in
+  ``"triton"`` mode (the same fp32 divisions); the default ``"torch"`` mode is bit-exact
+  with ``blockwise_quantize_torch`` (``test_quant_gpu.py``) and its disagreement with
+  the Triton kernel is measured and bounded here.
+* GEMM: relative Frobenius <= 1e-2 and |D - ref| <= 2e-2 + 1 bf16 ulp(|ref|) element by
+  element against the exact dequantise-then-fp32-matmul; our error no larger than the
+  SM89 kernel's; and the two kernels within that element bound of each other.
+* producers and RoPE: agreement with the reference kernels measured and bounded (the
+  reference compiles them with fast-math exp / rsqrt, which the product does not
+  restate bit for bit).
+"""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import activations, bias as make_bias, bits, scales_mn, weights
+from oracle import oracle as O
+from oracle import refpath
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not refpath.available(), reason="oracle/_ref (the reference's build) not present")]
+
+REL_FRO = 1e-2
+ABS_TOL = 2e-2  # plus one bf16 ulp of |ref|, element by element
+
+
+# ----------------------------------------------------------------------------- comparison helpers
+def _codes_eq(a, b):
+    a, b = a.reshape(-1).view(torch.uint8), b.reshape(-1).view(torch.uint8)
+    nan = ((a & 0x7F) == 0x7F) & ((b & 0x7F) == 0x7F)
+    return (a == b) | nan
+
+
+def _f32_eq(a, b):
+    a, b = a.contiguous().reshape(-1), b.contiguous().reshape(-1)
+    return (a.view(torch.int32) == b.view(torch.int32)) | (torch.isnan(a) & torch.isnan(b))
+
+
+def _bf16_eq(a, b):
+    a, b = a.contiguous().reshape(-1), b.contiguous().reshape(-1)
+    return (a.view(torch.int16) == b.view(torch.int16)) | (torch.isnan(a) & torch.isnan(b))
+
+
+def _bf16_ulps(a, b):
+    """Distance in bf16 ulps between finite values (ordered integer encoding)."""
+    def ordered(t):
+        i = t.contiguous().reshape(-1).view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+    return (ordered(a) - ordered(b)).abs()
+
+
+def _device_acts(M, K, dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, generator=g, device=dev)
+    x[:, torch.randperm(K, generator=g, device=dev)[: max(1, K // 100)]] *= 20.0
+    return x.to(torch.bfloat16)
+
+
+def _report(name, **kv):
+    print(f"[ref-parity] {name} " + json.dumps({k: (round(v, 8) if isinstance(v, float) else v) for k, v in kv.items()}))
+
+
+# ----------------------------------------------------------------------------- quantiser
+@pytest.mark.parametrize("M,K", [(6144, 4096), (333, 2048), (24576, 16384)])
+def test_quantizer_vs_reference_triton(cuda_device, M, K):
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
+    T = refpath.triton_ops()
+    x = _device_acts(M, K, cuda_device, seed=M + K)
+    rq, rs = T._quant_blockwise_tma_aligned_func(x.view(1, M, K), False)
+    tq, ts = ops.quantize_1x128(x, L.QUANT_TRITON)
+    oq, os_ = ops.quantize_1x128(x, L.QUANT_TORCH)
+    torch.cuda.synchronize()
+    tri_codes, tri_scales = _codes_eq(tq, rq), _f32_eq(ts, rs)
+    tor_codes, tor_scales = _codes_eq(oq, rq), _f32_eq(os_, rs)
+    _report(f"quant {M}x{K}", triton_mode_code_mismatch=1 - tri_codes.float().mean().item(),
+            triton_mode_scale_mismatch=1 - tri_scales.float().mean().item(),
+            torch_mode_code_mismatch=1 - tor_codes.float().mean().item(),
+            torch_mode_scale_mismatch=1 - tor_scales.float().mean().item())
+    assert bool(tri_codes.all()) and bool(tri_scales.all())
+    # torch-mode scales are one IEEE reciprocal-and-multiply away from Triton's approximate divisions
+    assert 1 - tor_scales.float().mean().item() < 0.5
+    assert 1 - tor_codes.float().mean().item() < 0.02
+
+
+def test_quantizer_edge_rows_vs_reference_triton(cuda_device):
+    """Zero, infinite, NaN, tiny and huge groups: agreement with the Triton kernel reported
+    per row; finite rows must match in triton mode."""
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
+    T = refpath.triton_ops()
+    K = 512
+    x = activations(12, K, seed=5).float()
+    x[0] = 0.0
+    x[1, 5] = float("inf")
+    x[2, 130] = float("-inf")
+    x[3, 7] = float("nan")
+    x[4] *= 1e-30
+    x[5] *= 1e30
+    x[6, :128] = -0.0
+    x[7, :] = 448.0
+    x = x.to(torch.bfloat16).to(cuda_device)
+    rq, rs = T._quant_blockwise_tma_aligned_func(x.view(1, 12, K), False)
+    tq, ts = ops.quantize_1x128(x, L.QUANT_TRITON)
+    torch.cuda.synchronize()
+    per_row = {}
+    for r in range(12):
+        per_row[r] = (bool(_codes_eq(tq[r], rq.view(12, K)[r]).all()), bool(_f32_eq(ts[r], rs[r]).all()))
+    _report("quant edge rows (codes equal, scales equal)", rows=per_row)
+    for r in (0, 4, 5, 6, 7, 8, 9, 10, 11):
+        assert per_row[r] == (True, True), (r, per_row[r])
+
+
+# ----------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(6144, 4096, 4096), (333, 1024, 2048), (24576, 16384, 4096),
+                                   (24576, 4096, 16384)])
+def test_gemm_vs_reference_sm89(cuda_device, M, N, K):
+    from ltx_kernels.blockwise import ops
+    G = refpath.gemm()
+    x = _device_acts(M, K, cuda_device, seed=7 * M + K)
+    g = torch.Generator(device=cuda_device).manual_seed(N + K)
+    w = torch.randn(N, K, generator=g, device=cuda_device) * 0.02
+    b = (torch.randn(N, generator=g, device=cuda_device) * 0.01).to(torch.bfloat16).float()
+    aq, asc = ops.quantize_1x128(x)
+    wq, wsc = ops.quantize_weight_128x128(w)
+    d_ref = torch.empty((M, N), dtype=torch.bfloat16, device=cuda_device)
+    G.fp8_gemm_nt_sm89((aq, asc), (wq, wsc), d_ref, b, use_fast_accum=False)
+    d = ops.gemm(aq, asc, wq, wsc, b)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    rows = np.unique(np.concatenate([np.random.default_rng(M).choice(M, size=min(M, 48), replace=False),
+                                     [0, M - 1]]))
+    ri = torch.from_numpy(rows).to(cuda_device)
+    exact = O.gemm_dequant_f32(bits(aq[ri]), scales_mn(asc, M)[:, rows], bits(wq), wsc.cpu().numpy(),
+                               b.cpu().numpy())
+    m_ours = O.error_metrics(O.bf16_to_f32(bits(d[ri])), exact, abs_tol=ABS_TOL)
+    m_ref = O.error_metrics(O.bf16_to_f32(bits(d_ref[ri])), exact, abs_tol=ABS_TOL)
+    same = _bf16_eq(d, d_ref).float().mean().item()
+    ulps = _bf16_ulps(d, d_ref)
+    _report(f"gemm {M}x{N}x{K}", ours=m_ours, sm89=m_ref, bitwise_equal_frac=same,
+            max_ulp_vs_sm89=int(ulps.max().item()), frac_gt1ulp=(ulps > 1).float().mean().item())
+    assert m_ours["rel_fro"] <= REL_FRO and m_ours["bound_excess"] <= 0, m_ours
+    assert m_ours["rel_fro"] <= 1.05 * m_ref["rel_fro"] + 1e-5, (m_ours, m_ref)
+    both = O.error_metrics(O.bf16_to_f32(bits(d)), O.bf16_to_f32(bits(d_ref)), abs_tol=ABS_TOL)
+    assert both["bound_excess"] <= 0, both
+
+
+def test_ffn_chain_vs_reference_chain(cuda_device):
+    """Config-1 FFN at 4096 tokens: the reference's chain (Triton quant, SM89 up with bias,
+    torch GELU-tanh on bf16, Triton requant, SM89 down) against ours (quant, up GEMM with
+    fused GELU + requant, down GEMM), both against the exact chain."""
+    import torch.nn.functional as F
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
+    G, T = refpath.gemm(), refpath.triton_ops()
+    M, D, H = 4096, 4096, 16384
+    x = _device_acts(M, D, cuda_device, seed=99)
+    g = torch.Generator(device=cuda_device).manual_seed(100)
+    w1q, w1s = ops.quantize_weight_128x128(torch.randn(H, D, generator=g, device=cuda_device) * 0.02)
+    w2q, w2s = ops.quantize_weight_128x128(torch.randn(D, H, generator=g, device=cuda_device) * 0.02)
+    b1 = (torch.randn(H, generator=g, device=cuda_device) * 0.01).to(torch.bfloat16).float()
+    b2 = (torch.randn(D, generator=g, device=cuda_device) * 0.01).to(torch.bfloat16).float()
+    # reference chain
+    rq, rs = T._quant_blockwise_tma_aligned_func(x.view(1, M, D), False)
+    h_ref = torch.empty((M, H), dtype=torch.bfloat16, device=cuda_device)
+    G.fp8_gemm_nt_sm89((rq.view(M, D), rs), (w1q, w1s), h_ref, b1, use_fast_accum=False)
+    h_ref = F.gelu(h_ref, approximate="tanh")
+    hq_ref, hs_ref = T._quant_blockwise_tma_aligned_func(h_ref.view(1, M, H), False)
+    y_ref = torch.empty((M, D), dtype=torch.bfloat16, device=cuda_device)
+    G.fp8_gemm_nt_sm89((hq_ref.view(M, H), hs_ref), (w2q, w2s), y_ref, b2, use_fast_accum=False)
+    # ours (triton-mode quantisers, the same arithmetic as the reference's)
+    aq, asc = ops.quantize_1x128(x, L.QUANT_TRITON)
+    _, hq, hs = ops.gemm(aq, asc, w1q, w1s, b1, gelu=True, requant=True, write_d=False)
+    y = ops.gemm(hq, hs, w2q, w2s, b2)
+    torch.cuda.synchronize()
+    rows = np.arange(0, M, 97)
+    ri = torch.from_numpy(rows).to(cuda_device)
+    # exact chain on the sampled rows, from the reference's own quantised input
+    h_ex = O.gemm_dequant_f32(bits(rq.view(M, D)[ri]), scales_mn(rs, M)[:, rows], bits(w1q), w1s.cpu().numpy(),
+                              b1.cpu().numpy())
+    h_ex = O.gelu_tanh_bf16(O.f32_to_bf16(h_ex))
+    q_ex, s_ex = O.quant_act_1x128(h_ex)
+    y_ex = O.gemm_dequant_f32(q_ex, s_ex, bits(w2q), w2s.cpu().numpy(), b2.cpu().numpy())
+    m_ours = O.error_metrics(O.bf16_to_f32(bits(y[ri])), y_ex, abs_tol=ABS_TOL)
+    m_ref = O.error_metrics(O.bf16_to_f32(bits(y_ref[ri])), y_ex, abs_tol=ABS_TOL)
+    groups_same = _codes_eq(hq, hq_ref.view(M, H)).view(M, H // 128, 128).all(dim=2).float().mean().item()
+    _report("ffn chain 4096x4096->16384->4096", ours=m_ours, reference=m_ref, requant_groups_equal=groups_same)
+    assert m_ours["rel_fro"] <= REL_FRO and m_ours["bound_excess"] <= 0, m_ours
+    assert m_ours["rel_fro"] <= 1.05 * m_ref["rel_fro"] + 1e-5, (m_ours, m_ref)
+
+
+# ----------------------------------------------------------------------------- the reference's module on our GEMM
+_LINEAR_PROBE = r'''
+import json, sys, types, torch
+sys.path[:0] = [REF_PY]
+sys.path.insert(0, REPO)
+from oracle import refpath
+sys.modules["ops_cpp"] = refpath.ops()
+a2a = types.ModuleType("all2all_cpp"); a2a.All2All = None; sys.modules["all2all_cpp"] = a2a
+if MODE == "reference":
+    sys.modules["blockwise_cpp"] = refpath.gemm()
+else:
+    sys.path.insert(0, DROPIN)
+from ltx_kernels.blockwise.linear import BlockwiseFP8Linear
+import blockwise_cpp
+torch.manual_seed(0)
+lin = torch.nn.Linear(4096, 4096, bias=True).cuda()
+with torch.no_grad():
+    lin.weight.normal_(0, 0.02); lin.bias.normal_(0, 0.01)
+layer = BlockwiseFP8Linear.from_linear(lin)
+g = torch.Generator(device="cuda").manual_seed(1)
+x = torch.randn(2, 3000, 4096, generator=g, device="cuda")
+x[..., torch.randperm(4096, generator=g, device="cuda")[:40]] *= 20
+y = layer(x.to(torch.bfloat16))
+torch.cuda.synchronize()
+torch.save({"y": y.cpu(), "gemm_module": blockwise_cpp.__file__}, OUT)
+print("LINEAR_OK")
+'''
+
+
+def test_reference_linear_module_on_our_gemm(cuda_device, tmp_path):
+    """The reference's BlockwiseFP8Linear forward (its Triton quant, its dispatch) run once
+    with the reference's SM89 build as ``blockwise_cpp`` and once with this repository's
+    drop-in module: outputs within the GEMM element bound of each other."""
+    outs = {}
+    for mode in ("reference", "ours"):
+        out = tmp_path / f"{mode}.pt"
+        code = (f"REF_PY={refpath.PY_ROOT!r}\nREPO={REPO!r}\nDROPIN={os.path.join(REPO, 'ltx-2_b200', 'dropin')!r}\n"
+                f"MODE={mode!r}\nOUT={str(out)!r}\n" + _LINEAR_PROBE)
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=str(tmp_path))
+        assert r.returncode == 0 and "LINEAR_OK" in r.stdout, r.stderr[-3000:]
+        outs[mode] = torch.load(out)
+    assert outs["ours"]["gemm_module"].startswith(os.path.join(REPO, "ltx-2_b200", "dropin"))
+    assert "ref_blockwise_cpp" in outs["reference"]["gemm_module"]
+    ya, yb = outs["ours"]["y"], outs["reference"]["y"]
+    assert ya.shape == yb.shape == (2, 3000, 4096) and ya.dtype == torch.bfloat16
+    m = O.error_metrics(O.bf16_to_f32(bits(ya)), O.bf16_to_f32(bits(yb)), abs_tol=ABS_TOL)
+    _report("reference BlockwiseFP8Linear: our GEMM vs SM89", **m)
+    assert m["rel_fro"] <= REL_FRO and m["bound_excess"] <= 0, m
+
+
+# ----------------------------------------------------------------------------- producers and RoPE
+def _prod_inputs(dev, B=2, S=1000, H=4096, heads=32, seed=3):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    r = lambda *s, std=1.0: (torch.randn(*s, generator=g, device=dev) * std).to(torch.bfloat16)
+    return dict(x=r(B, S, H), y=r(B, S, H), sc=r(B, 1, H, std=0.1), sh=r(B, 1, H, std=0.1),
+                z=r(B, 1, H, std=0.1), logits=r(B, S, heads, std=3.0))
+
+
+def _q_agree(q, s, rq, rs):
+    M, H = q.shape[0], q.shape[-1]
+    codes = _codes_eq(q.reshape(M, H), rq.reshape(M, H))
+    groups = codes.view(M, H // 128, 128).all(dim=2)
+    return {"codes_equal": codes.float().mean().item(), "groups_equal": groups.float().mean().item(),
+            "scales_equal": _f32_eq(s, rs).float().mean().item()}
+
+
+def test_producers_vs_reference_triton(cuda_device):
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
+    T = refpath.triton_ops()
+    p = _prod_inputs(cuda_device)
+    B, S, H = p["x"].shape
+    res = {}
+    for mode_name, mode in (("torch", L.QUANT_TORCH), ("triton", L.QUANT_TRITON)):
+        rq, rs = T.run_quant_blockwise_norm_tma_aligned(p["x"], None, p["sc"], p["sh"], torch.float8_e4m3fn, None)
+        q, s = ops.adanorm_quantize(p["x"], p["sc"], p["sh"], mode)
+        res[f"adanorm/{mode_name}"] = _q_agree(q, s, rq, rs)
+        xr, xo = p["x"].clone(), p["x"].clone()
+        rq, rs = T.run_quant_blockwise_rms_fma(xr, p["y"], p["z"])
+        q, s = ops.rms_fma(xo, p["y"], p["z"], True, mode)
+        res[f"quant_rms_fma/{mode_name}"] = _q_agree(q, s, rq, rs)
+        res[f"quant_rms_fma/{mode_name}"]["x_updated_equal"] = _bf16_eq(xo, xr).float().mean().item()
+        rq, rs = T.run_gated_attention(p["x"], p["logits"], True)
+        q, s = ops.gated_attention(p["x"], p["logits"], True, mode)
+        res[f"gated_attention/{mode_name}"] = _q_agree(q, s, rq, rs)
+        rq, rs = T._quant_blockwise_tma_aligned_func(p["y"], True)
+        q, s = ops.gelu_quantize_1x128(p["y"], mode)
+        res[f"gelu_quant/{mode_name}"] = _q_agree(q, s, rq, rs)
+    xr, xo = p["x"].clone(), p["x"].clone()
+    r_out = T.run_rms_fma(xr, p["y"], p["z"])
+    o_out = ops.rms_fma(xo, p["y"], p["z"], False)
+    res["rms_fma_bf16"] = {"equal": _bf16_eq(o_out, r_out).float().mean().item(),
+                           "max_ulp": int(_bf16_ulps(o_out, r_out).max().item())}
+    r_out, _ = T.run_gated_attention(p["x"], p["logits"], False)
+    o_out = ops.gated_attention(p["x"], p["logits"], False)
+    res["gated_attention_bf16"] = {"equal": _bf16_eq(o_out, r_out).float().mean().item(),
+                                   "max_ulp": int(_bf16_ulps(o_out, r_out).max().item())}
+    torch.cuda.synchronize()
+    _report("producers vs reference Triton", **res)
+    for k, v in res.items():
+        if "codes_equal" in v:
+            assert v["codes_equal"] > 0.99 and v["scales_equal"] > 0.5, (k, v)
+        else:
+            assert v["equal"] > 0.99 and v["max_ulp"] <= 2, (k, v)
+
+
+def test_rope_vs_reference_ops_cpp(cuda_device):
+    from ltx_kernels.blockwise import ops
+    R = refpath.ops()
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    B, S, H, heads = 2, 500, 4096, 32
+    x = torch.randn(B, S, H, generator=g, device=cuda_device).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=cuda_device)).to(torch.bfloat16)
+    ang = torch.rand(B, S, H, generator=g, device=cuda_device) * 6.0
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    res = {}
+    for affine in (False, True):
+        for fp8 in (False, True):
+            r = R.rms_norm_rope(x, w if affine else None, cos, sin, not fp8)
+            o = ops.rms_norm_rope(x, cos, sin, w if affine else None, out_fp8=fp8)
+            key = f"rope/affine={affine}/fp8={fp8}"
+            if fp8:
+                res[key] = {"equal": _codes_eq(o, r).float().mean().item()}
+            else:
+                res[key] = {"equal": _bf16_eq(o, r).float().mean().item(),
+                            "max_ulp": int(_bf16_ulps(o, r).max().item())}
+    angs = torch.rand(B, heads, S, H // heads // 2, generator=g, device=cuda_device) * 6.0
+    cs, sn = angs.cos().to(torch.bfloat16), angs.sin().to(torch.bfloat16)
+    for fp8 in (False, True):
+        r = R.rms_norm_split_rope(x, sn, cs, w, fp8)
+        o = ops.rms_norm_split_rope(x, cs, sn, w, out_fp8=fp8)
+        key = f"split_rope/fp8={fp8}"
+        if fp8:
+            res[key] = {"equal": _codes_eq(o, r).float().mean().item()}
+        else:
+            res[key] = {"equal": _bf16_eq(o, r).float().mean().item(), "max_ulp": int(_bf16_ulps(o, r).max().item())}
+    torch.cuda.synchronize()
+    _report("rope vs reference ops_cpp", **res)
+    for k, v in res.items():
+        assert v["equal"] > 0.98, (k, v)
+        assert v.get("max_ulp", 0) <= 2, (k, v)
+
+
+def test_fp6_vs_reference_ops_cpp(cuda_device):
+    from ltx_kernels.blockwise import ops
+    R = refpath.ops()
+    g = torch.Generator(device=cuda_device).manual_seed(12)
+    codes = torch.randint(0, 256, (256, 4096), generator=g, device=cuda_device, dtype=torch.uint8)
+    codes &= 0x9F  # FP6 codes: the two top exponent bits zero
+    rp = R.fp6_pack(codes)
+    op = ops.fp6_pack(codes)
+    assert torch.equal(op, rp)
+    assert torch.equal(ops.fp6_unpack(op, 4096), R.fp6_unpack(rp, 4096))
