@@ -191,8 +191,15 @@ int ltxfp8_rms_norm_split_rope(const void* x, int64_t B, int64_t S, int64_t H, i
                                void* out, int out_fp8, void* stream);
 
 /* Epilogue options of ltxfp8_gemm (all zero = plain bias + bf16 store). */
+/* ltxfp8_epilogue.gelu_tanh */
+#define LTXFP8_GELU_NONE 0
+#define LTXFP8_GELU_TANH 1      /* torch's CUDA GELU-tanh, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) in fp32
+                                   with CUDA's tanhf, as F.gelu(approximate="tanh") computes it (gelu_approx.py:10) */
+#define LTXFP8_GELU_TANH_FAST 2 /* the same function as x / (1 + 2^a) with approximate exp2 and reciprocal:
+                                   no cancellation, within one bf16 ulp of LTXFP8_GELU_TANH */
+
 typedef struct ltxfp8_epilogue {
-  int gelu_tanh;          /* apply GELU (tanh approximation) to bf16(acc + bias), rounding to bf16 */
+  int gelu_tanh;          /* LTXFP8_GELU_*: apply GELU to bf16(acc + bias), rounding the result to bf16 */
   void* requant_q;        /* non-NULL: write the 1x128 e4m3 quantisation of the bf16 result, [M, N] */
   float* requant_scales;  /* its scales, element (m, nb) at requant_scales[nb * requant_ld + m] */
   int64_t requant_ld;     /* >= M */
@@ -203,6 +210,8 @@ typedef struct ltxfp8_epilogue {
   float lora_alpha;       /* scale of the LoRA term */
   void* workspace;        /* optional fp32 scratch for split-K on skinny M (see ltxfp8_gemm_workspace_bytes) */
   size_t workspace_bytes; /* its size; split-K is used only when it is large enough */
+  int requant_mode;       /* arithmetic of the requantisation's scales: LTXFP8_QUANT_TORCH (0) or
+                             LTXFP8_QUANT_TRITON, as for ltxfp8_quantize_1x128 */
 } ltxfp8_epilogue;
 
 /*

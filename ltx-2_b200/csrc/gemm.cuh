@@ -59,10 +59,31 @@ constexpr uint32_t kGemmLaunchRegs = 168;
 static_assert(128 * kRegsCtrl + 256 * kRegsEpi <= kGemmThreads * kGemmLaunchRegs, "register split exceeds launch");
 
 enum GemmFlags : int {
-  kGemmBias = 1,     // add fp32 bias[n]
-  kGemmWriteD = 2,   // write the bf16 result (the GELU output when GELU is on)
-  kGemmLora = 4,     // extra bf16 K blocks with scale lora_alpha
+  kGemmBias = 1,            // add fp32 bias[n]
+  kGemmWriteD = 2,          // write the bf16 result (the GELU output when GELU is on)
+  kGemmLora = 4,            // extra bf16 K blocks with scale lora_alpha
+  kGemmGeluFast = 8,        // GELU as x / (1 + 2^a) with approximate instructions (else torch's formula)
+  kGemmRequantTriton = 16,  // requantisation scales as the Triton quantiser computes them (div.full)
 };
+
+// bf16 GELU of a bf16 value held in fp32 (exact), rounded to bf16: torch's formula or
+// the fast form, chosen per launch (warp-uniform).
+__device__ __forceinline__ float2 gemm_gelu2(float2 x, bool fast) {
+  if (fast) return gelu_tanh_f32x2(x);
+  return make_float2(gelu_tanh_torch(x.x), gelu_tanh_torch(x.y));
+}
+
+// Scale pair of a requantised 1x128 group from its abs-max: the Triton quantiser's
+// divisions (triton_ops.py:19-21) or torch's reciprocal-multiply (functional.py:142-144).
+__device__ __forceinline__ void requant_scale(float amax, bool triton, float& s, float& inv) {
+  if (triton) {
+    s = div_full(448.0f, amax);
+    inv = div_full(1.0f, s);
+  } else {
+    s = __fmul_rn(__frcp_rn(amax), 448.0f);
+    inv = __frcp_rn(s);
+  }
+}
 
 // Device status codes recorded when a bounded wait gives up.
 enum GemmStatus : unsigned int {
@@ -348,8 +369,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
               __syncwarp();
             }
-            const float s = __fmul_rn(__frcp_rn(stg_amax[g * kBM + r]), 448.0f);
-            const bool in_range = isfinite(s);  // then no product exceeds 448: plain hardware conversion
+            float s, s_inv;
+            requant_scale(stg_amax[g * kBM + r], (p.flags & kGemmRequantTriton) != 0, s, s_inv);
+            // a finite scale keeps every product within 448 (plain hardware conversion); the
+            // Triton quantiser always converts with saturation
+            const bool in_range = isfinite(s) || (p.flags & kGemmRequantTriton) != 0;
             uint8_t* qrow = staging + (2 * g) * kStagingBlockBytes + r * 128;
 #pragma unroll 1
             for (int k = 0; k < 8; ++k) {  // 16 codes from bf16 chunks 2k, 2k+1
@@ -371,7 +395,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               // Code chunk k replaces bf16 chunk k of the block, already read (k <= 2k).
               *reinterpret_cast<uint4*>(qrow + ((k ^ (r & 7)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            if (m0 + r < p.M) p.s_out[static_cast<int64_t>(col0 / 128) * p.s_out_ld + m0 + r] = __frcp_rn(s);
+            if (m0 + r < p.M) p.s_out[static_cast<int64_t>(col0 / 128) * p.s_out_ld + m0 + r] = s_inv;
             __syncwarp();
             fence_proxy_async_smem();
             __syncwarp();
@@ -482,6 +506,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       const bool has_bias = (p.flags & kGemmBias) != 0 && col_ok;
+      const bool gelu_fast = (p.flags & kGemmGeluFast) != 0;
       const float4* bias4 = reinterpret_cast<const float4*>(p.bias + col0);
       const int r_local = sp * 32 + lane;
       float gmax = 0.0f;  // abs-max of this thread's 1x128 group (requant)
@@ -500,8 +525,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // rounds the result to bf16.
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float2 y =
-                gelu_tanh_f32x2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)));
+            const float2 y = gemm_gelu2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)),
+                                        gelu_fast);
             w4[i] = pack_bf16x2(y.x, y.y);
           }
         }
@@ -572,7 +597,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmParams p) 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float y = bf16_round(f[i]);
-      if constexpr (kGelu) y = bf16_round(gelu_tanh_f32(y));
+      if constexpr (kGelu) y = bf16_round((p.flags & kGemmGeluFast) ? gelu_tanh_f32(y) : gelu_tanh_torch(y));
       f[i] = y;
     }
   }
@@ -587,8 +612,9 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmParams p) 
     for (int i = 0; i < 8; ++i) amax = fmax_nan(amax, fabsf(f[i]));
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmax_nan(amax, __shfl_xor_sync(0xffffffffu, amax, o, 16));
-    const float s = __fmul_rn(__frcp_rn(amax), 448.0f);
-    const bool in_range = isfinite(s);
+    float s, s_inv;
+    requant_scale(amax, (p.flags & kGemmRequantTriton) != 0, s, s_inv);
+    const bool in_range = isfinite(s) || (p.flags & kGemmRequantTriton) != 0;
     uint32_t w[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -600,7 +626,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmParams p) 
     }
     if (active) {
       *reinterpret_cast<uint2*>(p.q_out + off) = make_uint2(w[0], w[1]);
-      if (l16 == 0) p.s_out[static_cast<int64_t>(grp) * p.s_out_ld + row] = __frcp_rn(s);
+      if (l16 == 0) p.s_out[static_cast<int64_t>(grp) * p.s_out_ld + row] = s_inv;
     }
   }
 }

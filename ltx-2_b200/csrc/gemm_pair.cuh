@@ -276,8 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               __syncwarp();
             }
-            const float s = __fmul_rn(__frcp_rn(stg_amax[g * kRowsPerCta + r]), 448.0f);
-            const bool in_range = isfinite(s);  // then no product exceeds 448: plain hardware conversion
+            float s, s_inv;
+            requant_scale(stg_amax[g * kRowsPerCta + r], (p.flags & kGemmRequantTriton) != 0, s, s_inv);
+            const bool in_range = isfinite(s) || (p.flags & kGemmRequantTriton) != 0;
             uint8_t* qrow = staging + (2 * g) * kStagingBlockBytes + r * 128;
 #pragma unroll 1
             for (int k = 0; k < 8; ++k) {  // 16 codes from bf16 chunks 2k, 2k+1
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // Code chunk k replaces bf16 chunk k of the block, already read (k <= 2k).
               *reinterpret_cast<uint4*>(qrow + ((k ^ (r & 7)) * 16)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            if (m0 + r < p.M) p.s_out[static_cast<int64_t>(col0 / 128) * p.s_out_ld + m0 + r] = __frcp_rn(s);
+            if (m0 + r < p.M) p.s_out[static_cast<int64_t>(col0 / 128) * p.s_out_ld + m0 + r] = s_inv;
             __syncwarp();
             fence_proxy_async_smem();
             __syncwarp();
@@ -390,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       const bool has_bias = (p.flags & kGemmBias) != 0 && col_ok;
+      const bool gelu_fast = (p.flags & kGemmGeluFast) != 0;
       const float4* bias4 = reinterpret_cast<const float4*>(p.bias + col0);
       float gmax = 0.0f;
 #pragma unroll
@@ -405,8 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (kGelu) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float2 y =
-                gelu_tanh_f32x2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)));
+            const float2 y = gemm_gelu2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)),
+                                        gelu_fast);
             w4[i] = pack_bf16x2(y.x, y.y);
           }
         }

@@ -821,7 +821,9 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
   p.s_out = e.requant_scales ? e.requant_scales + row0 : nullptr;
   p.s_out_ld = e.requant_ld;
   p.lora_alpha = e.lora_alpha;
-  p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0);
+  p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0) |
+            (e.gelu_tanh == LTXFP8_GELU_TANH_FAST ? kGemmGeluFast : 0) |
+            (e.requant_mode == LTXFP8_QUANT_TRITON ? kGemmRequantTriton : 0);
   p.k_splits = 1;
   p.kb_per_split = p.num_kb;
   p.ws = nullptr;
@@ -877,6 +879,10 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   if (write_d && !aligned(D, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: D must be 16-byte aligned");
   if (!aligned(sfa, 4) || !aligned(sfb, 4)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: scales must be 4-byte aligned");
   if (bias && !aligned(bias, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: bias must be 16-byte aligned");
+  if (e.gelu_tanh < LTXFP8_GELU_NONE || e.gelu_tanh > LTXFP8_GELU_TANH_FAST)
+    return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: unknown gelu_tanh mode %d", e.gelu_tanh);
+  if (e.requant_mode != LTXFP8_QUANT_TORCH && e.requant_mode != LTXFP8_QUANT_TRITON)
+    return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: unknown requant_mode %d", e.requant_mode);
   if (e.requant_q) {
     if (!e.requant_scales) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: requant_scales is null");
     if (e.requant_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: requant_ld < M");

@@ -12,11 +12,19 @@
 // Layout: one warp per token row (H <= 32 * 8 * kChunks bf16).  Lane l owns the
 // 16-byte chunks c = 32 i + l; a 1x128 group is 16 consecutive chunks, so load i
 // of lanes 0-15 is group 2i and of lanes 16-31 group 2i+1, and a group's abs-max
-// is a 16-lane shuffle reduction.  Row sums of squares are reduced in a fixed
-// order (lane-sequential over its chunks, then an xor butterfly 16, 8, 4, 2, 1),
-// and every other step is an IEEE-rounded operation (1/sqrt is sqrt then a
-// division, e^x is built from fused multiply-adds), so the CPU oracle
-// reproduces the outputs bit for bit.
+// is a 16-lane shuffle reduction.
+//
+// Two arithmetics (the template mode):
+//  * kQuantTriton -- the reference's kernels as Triton 3.6 compiles them for sm_100:
+//    bf16 operations where the Triton source keeps bf16 (its promotion rules), the
+//    bf16 row sum of squares in the order of Triton's reduction tree with the
+//    multiply-add fusion the compiler chose for each kernel, fused bf16 multiply-adds
+//    where it fuses them, and the instructions it emits (ex2.approx for exp, div.full
+//    for fp32 division, IEEE sqrt and division for rsqrt).  Checked against the
+//    reference's kernels on the B200 (GPU fixtures in tests/golden/ref_gpu_producers.npz).
+//  * kQuantTorch -- every step an IEEE-rounded operation (fp32 row sums in a fixed
+//    lane order, 1/sqrt as sqrt + division, e^x from fused multiply-adds), which the
+//    CPU oracle reproduces bit for bit.
 #pragma once
 
 #include "quant.cuh"
@@ -60,10 +68,74 @@ __device__ __forceinline__ float warp_sum_butterfly(float v) {
   return v;
 }
 
+// bf16x2 lanes of a 16-byte chunk.  bf16 sums and products computed in fp32 and
+// rounded once equal the correctly rounded bf16 operations: a product of two
+// bf16 values is exact in fp32, and a sum whose fp32 rounding is inexact has its
+// addends more than 16 binades apart, which keeps it off every bf16 midpoint.
+// So the packed __hadd2 / __hmul2_rn below compute bf16(a + b) and bf16(a * b)
+// (the _rn multiply keeps the compiler from contracting a product and a following
+// sum into one fused rounding).
+__device__ __forceinline__ __nv_bfloat162 bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ uint32_t u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ float2 f2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+__device__ __forceinline__ uint32_t word(const uint4& v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
+
 // 1/sqrt as an IEEE square root followed by an IEEE division.
 __device__ __forceinline__ float rsqrt_ieee(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
 
 __device__ __forceinline__ float bf16_rn(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// tl.exp on fp32 as Triton compiles it: 2^(x log2 e) with the product rounded first
+// and the approximate ex2 instruction.  (tl.rsqrt, by contrast, compiles to an IEEE
+// square root followed by an IEEE division: rsqrt_ieee.)
+__device__ __forceinline__ float exp_triton(float x) {
+  float r;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(x, 1.44269504088896341f)));
+  return r;
+}
+// tl.sigmoid(x) = 1 / (1 + exp(-x)) in fp32, the division being div.full.
+__device__ __forceinline__ float sigmoid_triton(float x) { return div_full(1.0f, __fadd_rn(1.0f, exp_triton(-x))); }
+
+// Row sum of squares the way the reference's Triton kernels reduce a bf16 row of
+// H = 1024 r elements (triton_ops.py:82-83, 220-221; Triton keeps tl.sum of a bf16
+// tensor in bf16).  The compiled kernel lays the row out as 4 warps x 32 lanes x 8
+// contiguous values per repetition: element r*1024 + t*8 + e is register j = 8r + e
+// of thread t.  Each thread sums its registers in order, every step rounded to bf16:
+// the first as bf16(x*x), later ones fused (acc = fma(x, x, acc), one rounding) or as
+// acc + bf16(x*x), following the fusion the compiler chose in that kernel (every
+// step in the AdaLN kernel, the even ones in the residual-FMA kernel).  The 32 lanes
+// of each warp then combine by an xor butterfly (16, 8, 4, 2, 1) and the four warps
+// as (w0 + w2) + (w1 + w3).  Lane l here plays threads w*32 + l, w = 0..3: its load i
+// (chunk 32 i + l) is repetition i/4 of thread (i%4)*32 + l.
+enum SumsqFusion : int { kFuseAll = 0, kFuseEven = 1 };
+
+template <int kFusion>
+__device__ __forceinline__ void triton_sumsq_chunk(__nv_bfloat16 (&acc)[4], int i, const uint4& v) {
+  const int w = i & 3, r = i >> 2;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t u = word(v, k);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_bfloat16 x = __ushort_as_bfloat16(static_cast<unsigned short>(h ? (u >> 16) : (u & 0xFFFFu)));
+      const int j = r * 8 + 2 * k + h;
+      if (j == 0)
+        acc[w] = __hmul_rn(x, x);
+      else if (kFusion == kFuseAll || (j & 1) == 0)
+        acc[w] = __hfma(x, x, acc[w]);
+      else
+        acc[w] = __hadd_rn(acc[w], __hmul_rn(x, x));
+    }
+  }
+}
+
+__device__ __forceinline__ float triton_sumsq_finish(__nv_bfloat16 (&acc)[4]) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int w = 0; w < 4; ++w) acc[w] = __hadd_rn(acc[w], __shfl_xor_sync(0xffffffffu, acc[w], off));
+  return __bfloat162float(__hadd_rn(__hadd_rn(acc[0], acc[2]), __hadd_rn(acc[1], acc[3])));
+}
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
@@ -104,17 +176,6 @@ __device__ __forceinline__ void quant_group8(const float (&f)[8], bool valid, ui
   }
 }
 
-// bf16x2 lanes of a 16-byte chunk.  bf16 sums and products computed in fp32 and
-// rounded once equal the correctly rounded bf16 operations: a product of two
-// bf16 values is exact in fp32, and a sum whose fp32 rounding is inexact has its
-// addends more than 16 binades apart, which keeps it off every bf16 midpoint.
-// So the packed __hadd2 / __hmul2_rn below compute bf16(a + b) and bf16(a * b)
-// (the _rn multiply keeps the compiler from contracting a product and a following
-// sum into one fused rounding).
-__device__ __forceinline__ __nv_bfloat162 bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
-__device__ __forceinline__ uint32_t u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ float2 f2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
-__device__ __forceinline__ uint32_t word(const uint4& v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
 
 struct ProducerOut {
   uint8_t* q;      // e4m3 [M, H] or null
@@ -152,15 +213,25 @@ __global__ void __launch_bounds__(kProdWarps * 32, 8) adanorm_quant_kernel(
   if (row >= M) return;
   const int nchunks = H / 8;
   const __nv_bfloat16* xr = x + row * H;
-  float acc = 0.0f;
+  // mean of the bf16 squares, + eps, 1/sqrt (triton_ops.py:82-85)
+  float r;
+  if constexpr (kMode == kQuantTriton) {
+    __nv_bfloat16 acc[4] = {};
 #pragma unroll
-  for (int i = 0; i < kChunks; ++i) {
-    const int c = i * 32 + lane;
-    if (c < nchunks) acc = sumsq_chunk(acc, ldg16(xr + c * 8));
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = i * 32 + lane;
+      if (c < nchunks) triton_sumsq_chunk<kFuseAll>(acc, i, ldg16(xr + c * 8));
+    }
+    r = rsqrt_ieee(__fadd_rn(div_full(triton_sumsq_finish(acc), static_cast<float>(H)), 1e-5f));
+  } else {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = i * 32 + lane;
+      if (c < nchunks) acc = sumsq_chunk(acc, ldg16(xr + c * 8));
+    }
+    r = rsqrt_ieee(__fadd_rn(__fdiv_rn(warp_sum_butterfly(acc), static_cast<float>(H)), 1e-5f));
   }
-  // mean of bf16 squares, + eps, 1/sqrt (triton_ops.py:82-85)
-  const float ss = warp_sum_butterfly(acc);
-  const float r = rsqrt_ieee(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), 1e-5f));
   const int64_t b = row / S, s = row - b * S;
   const __nv_bfloat16* scr = scale + b * scale_bs + s * scale_ss;
   const __nv_bfloat16* shr = shift + b * shift_bs + s * shift_ss;
@@ -180,10 +251,12 @@ __global__ void __launch_bounds__(kProdWarps * 32, 8) adanorm_quant_kernel(
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float2 xf = f2(bf2(word(xv, k)));
-      // (x * x_norm).to(bf16), then x * (1.0 + norm_scales) + norm_shift in bf16 steps
+      // (x * x_norm).to(bf16), then x * (1.0 + norm_scales) + norm_shift in bf16: the
+      // reference's compiled kernel fuses the last multiply-add (one rounding)
       const __nv_bfloat162 y = __float22bfloat162_rn(make_float2(__fmul_rn(xf.x, r), __fmul_rn(xf.y, r)));
       const __nv_bfloat162 t = __hadd2(one, bf2(word(sc, k)));
-      const float2 z = f2(__hadd2(__hmul2_rn(y, t), bf2(word(sh, k))));
+      const float2 z = kMode == kQuantTriton ? f2(__hfma2(y, t, bf2(word(sh, k))))
+                                             : f2(__hadd2(__hmul2_rn(y, t), bf2(word(sh, k))));
       f[2 * k] = z.x;
       f[2 * k + 1] = z.y;
     }
@@ -210,23 +283,34 @@ __global__ void __launch_bounds__(kProdWarps * 32, 8) rms_fma_kernel(__nv_bfloat
   const int64_t b = row / S, s = row - b * S;
   const __nv_bfloat16* zr = z + b * z_bs + s * z_ss;
   float acc = 0.0f;
+  __nv_bfloat16 tacc[4] = {};
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 32 + lane;
     if (c < nchunks) {
       const uint4 xv = *reinterpret_cast<const uint4*>(xr + c * 8);
       const uint4 yv = ldg16(yr + c * 8), zv = ldg16(zr + c * 8);
-      // bf16(x + bf16(y * z))
-      const uint4 ov = make_uint4(u32(__hadd2(bf2(xv.x), __hmul2_rn(bf2(yv.x), bf2(zv.x)))),
-                                  u32(__hadd2(bf2(xv.y), __hmul2_rn(bf2(yv.y), bf2(zv.y)))),
-                                  u32(__hadd2(bf2(xv.z), __hmul2_rn(bf2(yv.z), bf2(zv.z)))),
-                                  u32(__hadd2(bf2(xv.w), __hmul2_rn(bf2(yv.w), bf2(zv.w)))));
+      uint4 ov;
+      if constexpr (kMode == kQuantTriton) {
+        // x + y * z in bf16, fused by the reference's compiled kernel (one rounding)
+        ov = make_uint4(u32(__hfma2(bf2(yv.x), bf2(zv.x), bf2(xv.x))), u32(__hfma2(bf2(yv.y), bf2(zv.y), bf2(xv.y))),
+                        u32(__hfma2(bf2(yv.z), bf2(zv.z), bf2(xv.z))), u32(__hfma2(bf2(yv.w), bf2(zv.w), bf2(xv.w))));
+        triton_sumsq_chunk<kFuseEven>(tacc, i, ov);
+      } else {
+        // bf16(x + bf16(y * z))
+        ov = make_uint4(u32(__hadd2(bf2(xv.x), __hmul2_rn(bf2(yv.x), bf2(zv.x)))),
+                        u32(__hadd2(bf2(xv.y), __hmul2_rn(bf2(yv.y), bf2(zv.y)))),
+                        u32(__hadd2(bf2(xv.z), __hmul2_rn(bf2(yv.z), bf2(zv.z)))),
+                        u32(__hadd2(bf2(xv.w), __hmul2_rn(bf2(yv.w), bf2(zv.w)))));
+        acc = sumsq_chunk(acc, ov);
+      }
       *reinterpret_cast<uint4*>(xr + c * 8) = ov;  // residual stream updated in place
-      acc = sumsq_chunk(acc, ov);
     }
   }
-  const float ss = warp_sum_butterfly(acc);
-  const float r = rsqrt_ieee(__fdiv_rn(ss, static_cast<float>(H)));  // no epsilon (triton_ops.py:222-224)
+  // no epsilon (triton_ops.py:222-224)
+  const float r = kMode == kQuantTriton
+                      ? rsqrt_ieee(div_full(triton_sumsq_finish(tacc), static_cast<float>(H)))
+                      : rsqrt_ieee(__fdiv_rn(warp_sum_butterfly(acc), static_cast<float>(H)));
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 32 + lane;
@@ -269,7 +353,7 @@ __global__ void __launch_bounds__(kProdWarps * 32, 8) gated_attention_kernel(con
       } else {
         g = __bfloat162float(static_cast<const __nv_bfloat16*>(gate_logits)[row * heads + h]);
       }
-      const float gate = __fmul_rn(2.0f, sigmoid_cw(g));
+      const float gate = __fmul_rn(2.0f, kMode == kQuantTriton ? sigmoid_triton(g) : sigmoid_cw(g));
       if (part == 0) gate_lo = gate; else gate_hi = gate;
     }
   }
@@ -319,7 +403,10 @@ __global__ void __launch_bounds__(256) gelu_quant_kernel(const __nv_bfloat16* __
     float f[8];
     bf16x8_to_f32(v[u], f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = __fmul_rn(f[j], sigmoid_cw(__fmul_rn(1.702f, f[j])));
+    for (int j = 0; j < 8; ++j) {
+      const float a = __fmul_rn(1.702f, f[j]);
+      f[j] = __fmul_rn(f[j], kMode == kQuantTriton ? sigmoid_triton(a) : sigmoid_cw(a));
+    }
     const bool valid = row_ok && kb < KB;
     quant_group8<kMode>(f, valid, q + row * q_ld + kb * 128 + l16 * 8, sfa + kb * sfa_ld + row, l16);
   }

@@ -365,8 +365,21 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 
-// GELU with the tanh approximation, the function torch evaluates for
-// F.gelu(x, approximate="tanh"): 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3).
+// GELU with the tanh approximation exactly as torch's CUDA kernel evaluates it for
+// F.gelu(x, approximate="tanh") on a bf16 tensor (opmath fp32, then rounded to bf16):
+// kBeta = sqrt(2) * (2 / sqrt(pi)) / 2 and kKappa = 0.044715 as fp32 constants,
+//   0.5 * x * (1 + tanh(kBeta * (x + kKappa * x^3)))
+// with CUDA's tanhf, written with the same operations in the same order so that
+// the compiler forms the same fused multiply-add (x + kKappa * x^3).
+__device__ __forceinline__ float gelu_tanh_torch(float x) {
+  constexpr float kBeta = 0.7978845608028654f;
+  constexpr float kKappa = 0.044715f;
+  const float x_cube = x * x * x;
+  const float inner = kBeta * (x + kKappa * x_cube);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+// The same function, 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3),
 // Evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)), i.e.
 // gelu = x / (1 + 2^a) with the exponent folded into one base-2 argument
 // a = x (c1 + c3 x^2), c1 = -2 sqrt(2/pi) log2(e), c3 = 0.044715 c1, and the

@@ -24,6 +24,10 @@ ERR_DEVICE_STATUS = -6
 QUANT_TORCH = 0
 QUANT_TRITON = 1
 
+GELU_NONE = 0
+GELU_TANH = 1       # torch's CUDA GELU-tanh formula (bit-identical bf16 results)
+GELU_TANH_FAST = 2  # x / (1 + 2^a) with approximate instructions (within one bf16 ulp)
+
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
@@ -53,6 +57,7 @@ class Epilogue(ctypes.Structure):
         ("lora_alpha", ctypes.c_float),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("requant_mode", ctypes.c_int),
     ]
 
 

@@ -10,9 +10,13 @@ functional.py and triton_ops.py (ltx_core/quantization/blockwise/_impl.py:12-23)
 * ``blockwise_quantize_weights`` / ``fp8_blockwise_quantize_weights_torch`` --
   128x128 weight quantisation (functional.py:128-135,149-150), bit-exact.
 
-The activation quantiser's arithmetic is selectable (``set_quant_mode``):
-``"torch"`` (default) is bit-exact with the reference's ``blockwise_quantize_torch``;
-``"triton"`` reproduces the Triton kernel's division instruction.
+The arithmetic of every quantising op here, and of the fused GEMM epilogue's
+requantisation in ``fused.py``, is selectable (``set_quant_mode``):
+``"triton"`` (default) is the reference's GPU path -- its Triton kernels as compiled
+for the B200 (the same divisions, exp, bf16 steps and reduction order);
+``"torch"`` uses IEEE-rounded arithmetic throughout and is bit-exact with the
+reference's CPU function ``blockwise_quantize_torch`` and with the CPU oracle's
+restatement of the producers.
 
 * ``blockwise::adanorm``, ``blockwise::quant_rms_fma``, ``blockwise::rms_fma``,
   ``blockwise::gated_attention`` and ``blockwise::quantize(use_gelu=True)`` -- the
@@ -36,17 +40,24 @@ from . import ops
 FP8_SCALE_MAX = 448.0
 FP6_SCALE_MAX = 0.1172
 
-_QUANT_MODE = L.QUANT_TORCH
+_QUANT_MODE = L.QUANT_TRITON
 
 
 def set_quant_mode(mode: str) -> None:
-    """Select the activation quantiser's arithmetic: ``"torch"`` or ``"triton"``."""
+    """Select the quantising ops' arithmetic (process-wide): ``"triton"`` (the
+    reference's GPU kernels, the default) or ``"torch"`` (IEEE, the reference's CPU
+    function)."""
     global _QUANT_MODE
     _QUANT_MODE = {"torch": L.QUANT_TORCH, "triton": L.QUANT_TRITON}[mode]
 
 
 def get_quant_mode() -> str:
     return "triton" if _QUANT_MODE == L.QUANT_TRITON else "torch"
+
+
+def quant_mode_code() -> int:
+    """The current mode as the C ABI's LTXFP8_QUANT_* value."""
+    return _QUANT_MODE
 
 
 @torch.library.custom_op("blockwise::quantize", mutates_args=())

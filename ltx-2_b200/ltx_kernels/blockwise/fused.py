@@ -19,7 +19,7 @@ import torch
 import torch.nn as nn
 
 from . import ops
-from .functional import blockwise_quantize_triton
+from .functional import blockwise_quantize_triton, quant_mode_code
 from .linear import BlockwiseFP8Linear
 
 Activation = Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]
@@ -31,7 +31,7 @@ def _as_quantized(x: Activation) -> Tuple[torch.Tensor, torch.Tensor, tuple]:
         lead = tuple(q.shape[:-1])
         return q.reshape(-1, q.shape[-1]), s, lead
     lead = tuple(x.shape[:-1])
-    q, s = ops.quantize_1x128(x)
+    q, s = ops.quantize_1x128(x, quant_mode_code())
     return q, s, lead
 
 
@@ -44,6 +44,9 @@ def fp8_linear(x: Activation, weight: torch.Tensor, weight_scale: torch.Tensor, 
     ``lora = (A [r, K] bf16, B [N, r] bf16, alpha)`` adds ``alpha * B (A x)``; it needs
     the bf16 input (``x`` itself, or ``x_bf16`` when ``x`` is pre-quantised).
     Returns bf16 ``[..., N]``, or with ``requant`` a tuple ``(bf16 or None, e4m3, scales)``.
+    ``gelu=True`` is torch's GELU-tanh (the reference applies ``F.gelu(approximate="tanh")``
+    to the bf16 output, gelu_approx.py:10); the input quantisation and the requantisation
+    use the arithmetic of ``functional.set_quant_mode`` (default: the reference's GPU kernels).
     """
     ax = lb = None
     alpha = 1.0
@@ -55,7 +58,7 @@ def fp8_linear(x: Activation, weight: torch.Tensor, weight_scale: torch.Tensor, 
         ax = ops.lora_a(src, la)
     q, s, lead = _as_quantized(x)
     res = ops.gemm(q, s, weight, weight_scale, bias, gelu=gelu, requant=requant, write_d=write_d,
-                   lora_ax=ax, lora_b=lb, lora_alpha=alpha)
+                   lora_ax=ax, lora_b=lb, lora_alpha=alpha, requant_mode=quant_mode_code())
     N = weight.shape[0]
     if requant:
         d, qo, so = res

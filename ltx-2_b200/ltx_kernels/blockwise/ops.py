@@ -339,15 +339,19 @@ def rms_norm_split_rope(x: torch.Tensor, cos_freqs: torch.Tensor, sin_freqs: tor
 # ----------------------------------------------------------------------------- GEMM
 def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Tensor,
          bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,
-         gelu: bool = False, requant: bool = False, write_d: bool = True,
+         gelu=False, requant: bool = False, write_d: bool = True,
          lora_ax: Optional[torch.Tensor] = None, lora_b: Optional[torch.Tensor] = None,
-         lora_alpha: float = 1.0, split_k: bool = True):
+         lora_alpha: float = 1.0, split_k: bool = True, requant_mode: int = L.QUANT_TORCH):
     """Blockwise FP8 GEMM with fused epilogue.
 
-    Returns D (bf16 [M, N]) when ``requant`` is False, else ``(D or None, q, scales)``
-    where ``q``/``scales`` are the 1x128 quantisation of the (GELU'd) bf16 output in
-    the same layout blockwise::quantize produces.  Skinny shapes get a split-K
-    workspace from the caching allocator unless ``split_k`` is False."""
+    ``gelu``: False, True (torch's GELU-tanh formula, bf16 results identical to
+    ``F.gelu(approximate="tanh")``) or ``"fast"`` (the same function through
+    approximate instructions, within one bf16 ulp).  Returns D (bf16 [M, N]) when
+    ``requant`` is False, else ``(D or None, q, scales)`` where ``q``/``scales`` are the
+    1x128 quantisation of the (GELU'd) bf16 output in the layout blockwise::quantize
+    produces, with ``requant_mode``'s arithmetic (QUANT_TORCH or QUANT_TRITON).
+    Skinny shapes get a split-K workspace from the caching allocator unless
+    ``split_k`` is False."""
     _require_cuda("gemm", a_q, sfa, w_q, sfb, bias, lora_ax, lora_b)
     if a_q.dim() != 2 or w_q.dim() != 2:
         raise RuntimeError("gemm expects 2-D operands")
@@ -375,7 +379,15 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
     else:
         d = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a_q.device)
     ep = L.Epilogue()
-    ep.gelu_tanh = 1 if gelu else 0
+    if gelu == "fast":
+        ep.gelu_tanh = L.GELU_TANH_FAST
+    elif gelu is True or gelu == "tanh":
+        ep.gelu_tanh = L.GELU_TANH
+    elif gelu is False or gelu is None:
+        ep.gelu_tanh = L.GELU_NONE
+    else:
+        raise RuntimeError(f"gemm: gelu must be False, True or 'fast', got {gelu!r}")
+    ep.requant_mode = requant_mode
     q = s = None
     if requant:
         q = torch.empty((M, N), dtype=torch.float8_e4m3fn, device=a_q.device)

@@ -122,14 +122,18 @@ def test_gelu_quant_bit_exact(cuda_device, M, K):
 
 
 def test_producer_custom_ops(cuda_device):
-    """The reference's op names and Python entry points return what the kernels do."""
+    """The reference's op names and Python entry points return what the kernels do in the
+    functional layer's arithmetic (default: the reference's GPU kernels, triton mode)."""
     import ltx_kernels.blockwise.functional as F
+    from ltx_kernels import _lib as L
     from ltx_kernels.blockwise import ops
+    assert F.get_quant_mode() == "triton" and F.quant_mode_code() == L.QUANT_TRITON
+    mode = F.quant_mode_code()
     B, S, H = 2, 19, 2048
     x = _x(B, S, H, seed=9).to(cuda_device)
     sc, sh = _param(B, 1, H, seed=10).to(cuda_device), _param(B, 1, H, seed=11).to(cuda_device)
     q, s = F.blockwise_quantize_adanorm_triton(x, None, sc, sh, torch.float8_e4m3fn, 1.0)
-    q2, s2 = ops.adanorm_quantize(x, sc, sh)
+    q2, s2 = ops.adanorm_quantize(x, sc, sh, mode)
     assert q.shape == (B, S, H) and s.shape == (B * S, H // 128) and s.stride() == (1, 40)
     assert torch.equal(q.view(torch.uint8).view(B * S, H), q2.view(torch.uint8))
     assert torch.equal(s, s2)
@@ -137,7 +141,7 @@ def test_producer_custom_ops(cuda_device):
     y = _x(B, S, H, seed=12).to(cuda_device)
     xa, xb = x.clone(), x.clone()
     q, s = F.blockwise_quantize_rms_fma_triton(xa, y, sc)
-    q2, s2 = ops.rms_fma(xb, y, sc, True)
+    q2, s2 = ops.rms_fma(xb, y, sc, True, mode)
     assert torch.equal(xa, xb) and not torch.equal(xa, x)
     assert torch.equal(q.view(torch.uint8).view(B * S, H), q2.view(torch.uint8)) and torch.equal(s, s2)
     out = F.rms_fma_triton(x.clone(), y, sc)
@@ -150,12 +154,15 @@ def test_producer_custom_ops(cuda_device):
     assert none is None and out.dtype == torch.bfloat16 and out.shape == (B, S, H)
 
     q, s = torch.ops.blockwise.quantize(x, True)
-    q2, s2 = ops.gelu_quantize_1x128(x)
+    q2, s2 = ops.gelu_quantize_1x128(x, mode)
     assert torch.equal(q.view(torch.uint8).view(B * S, H), q2.view(torch.uint8)) and torch.equal(s, s2)
 
 
-def test_producers_triton_mode_close(cuda_device):
-    """The Triton-division quantiser mode moves codes by at most one step."""
+def test_producers_two_arithmetics_close(cuda_device):
+    """The triton mode (the reference's kernels: bf16 row sums in Triton's order, checked
+    against them by test_ref_fixtures_gpu.py) and the IEEE torch mode (fp32 sums, pinned
+    by the oracle) quantise the same normalised values: their dequantised outputs agree
+    to well within one e4m3 step, and most codes are identical."""
     from ltx_kernels import _lib as L
     from ltx_kernels.blockwise import ops
     B, S, H = 1, 256, 4096
@@ -163,12 +170,10 @@ def test_producers_triton_mode_close(cuda_device):
     sc, sh = _param(B, 1, H, seed=14).to(cuda_device), _param(B, 1, H, seed=15).to(cuda_device)
     qa, sa = ops.adanorm_quantize(x, sc, sh, L.QUANT_TORCH)
     qb, sb = ops.adanorm_quantize(x, sc, sh, L.QUANT_TRITON)
-    da, db = qa.view(torch.uint8).long(), qb.view(torch.uint8).long()
-    assert (da - db).abs().max().item() <= 1
-    assert (da == db).float().mean().item() > 0.99
-    ua = sa.t().contiguous().view(torch.int32).long()
-    ub = sb.t().contiguous().view(torch.int32).long()
-    assert (ua - ub).abs().max().item() <= 4
+    assert (qa.view(torch.uint8) == qb.view(torch.uint8)).float().mean().item() > 0.9
+    da, db = ops.dequantize_1x128(qa, sa).float(), ops.dequantize_1x128(qb, sb).float()
+    rel = ((da - db).norm() / da.norm()).item()
+    assert rel < 2e-2, rel
 
 
 def _rope_tables(shape, seed):

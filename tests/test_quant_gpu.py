@@ -52,13 +52,26 @@ def test_quant_scale_layout_and_strided_input(cuda_device):
 
 
 def test_quant_op_and_torch_variant(cuda_device):
+    """blockwise::quantize runs the functional layer's arithmetic (default: triton, the
+    reference's GPU kernel); blockwise_quantize_torch is always the torch arithmetic."""
     import ltx_kernels.blockwise.functional as F
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
     x = activations(2 * 17, 512, seed=9).view(2, 17, 512).to(cuda_device)
     q, s = torch.ops.blockwise.quantize(x, False)
-    q2, s2 = F.blockwise_quantize_torch(x)
+    qt, st = ops.quantize_1x128(x, L.QUANT_TRITON)
     assert q.shape == (2, 17, 512) and s.shape == (34, 4)
-    assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
-    assert torch.equal(s.t(), s2)
+    assert torch.equal(q.view(torch.uint8).view(34, 512), qt.view(torch.uint8)) and torch.equal(s, st)
+    q2, s2 = F.blockwise_quantize_torch(x)
+    q3, s3 = ops.quantize_1x128(x, L.QUANT_TORCH)
+    assert torch.equal(q2.view(torch.uint8).view(34, 512), q3.view(torch.uint8))
+    assert torch.equal(s2, s3.t())
+    F.set_quant_mode("torch")
+    try:
+        q4, s4 = torch.ops.blockwise.quantize(x, False)
+    finally:
+        F.set_quant_mode("triton")
+    assert torch.equal(q4.view(torch.uint8).view(34, 512), q3.view(torch.uint8)) and torch.equal(s4, s3)
     qg, sg = torch.ops.blockwise.quantize(x, True)  # GELU (sigmoid form) before the quantiser
     assert qg.shape == (2, 17, 512) and not torch.equal(qg.view(torch.uint8), q.view(torch.uint8))
 
