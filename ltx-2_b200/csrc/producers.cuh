@@ -20,8 +20,11 @@
 //    bf16 row sum of squares in the order of Triton's reduction tree with the
 //    multiply-add fusion the compiler chose for each kernel, fused bf16 multiply-adds
 //    where it fuses them, and the instructions it emits (ex2.approx for exp, div.full
-//    for fp32 division, IEEE sqrt and division for rsqrt).  Checked against the
-//    reference's kernels on the B200 (GPU fixtures in tests/golden/ref_gpu_producers.npz).
+//    for fp32 division, libdevice's rsqrtf).  Checked against the reference's kernels
+//    on the B200 (GPU fixtures in tests/golden/ref_gpu_producers.npz): bit-exact except
+//    where the fp32 1/sqrt reaches a quantised output unrounded (the quantised
+//    residual-FMA path) and a few rows whose bf16 row sum the compiled kernel rounds
+//    differently (rates stated in the tests).
 //  * kQuantTorch -- every step an IEEE-rounded operation (fp32 row sums in a fixed
 //    lane order, 1/sqrt as sqrt + division, e^x from fused multiply-adds), which the
 //    CPU oracle reproduces bit for bit.
@@ -86,8 +89,9 @@ __device__ __forceinline__ float rsqrt_ieee(float x) { return __fdiv_rn(1.0f, __
 __device__ __forceinline__ float bf16_rn(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // tl.exp on fp32 as Triton compiles it: 2^(x log2 e) with the product rounded first
-// and the approximate ex2 instruction.  (tl.rsqrt, by contrast, compiles to an IEEE
-// square root followed by an IEEE division: rsqrt_ieee.)
+// and the approximate ex2 instruction.  tl.rsqrt is libdevice's rsqrtf, which Triton
+// links and CUDA's rsqrtf also is (the closest match measured against the reference's
+// kernels; see the producer fixtures' tests).
 __device__ __forceinline__ float exp_triton(float x) {
   float r;
   asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(x, 1.44269504088896341f)));
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(kProdWarps * 32, 8) adanorm_quant_kernel(
       const int c = i * 32 + lane;
       if (c < nchunks) triton_sumsq_chunk<kFuseAll>(acc, i, ldg16(xr + c * 8));
     }
-    r = rsqrt_ieee(__fadd_rn(div_full(triton_sumsq_finish(acc), static_cast<float>(H)), 1e-5f));
+    r = rsqrtf(__fadd_rn(div_full(triton_sumsq_finish(acc), static_cast<float>(H)), 1e-5f));
   } else {
     float acc = 0.0f;
 #pragma unroll
@@ -309,7 +313,7 @@ __global__ void __launch_bounds__(kProdWarps * 32, 8) rms_fma_kernel(__nv_bfloat
   }
   // no epsilon (triton_ops.py:222-224)
   const float r = kMode == kQuantTriton
-                      ? rsqrt_ieee(div_full(triton_sumsq_finish(tacc), static_cast<float>(H)))
+                      ? rsqrtf(div_full(triton_sumsq_finish(tacc), static_cast<float>(H)))
                       : rsqrt_ieee(__fdiv_rn(warp_sum_butterfly(acc), static_cast<float>(H)));
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
