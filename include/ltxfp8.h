@@ -161,6 +161,17 @@ int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld
                                int64_t sfa_ld, int flags, void* stream);
 
 /*
+ * torch's GELU-tanh + quant: y = bf16 result of F.gelu(x, approximate="tanh") on the
+ * bf16 input, then the 1x128 quant of y; arguments as ltxfp8_quantize_1x128.
+ * Replaces the reference FFN's unfused chain after the up projection: F.gelu
+ * (ltx-core/src/ltx_core/model/transformer/gelu_approx.py:10) on the bf16 GEMM output,
+ * then blockwise::quantize in the down projection (ltx-kernels/.../linear.py:91-93).
+ * Codes and scales equal ltxfp8_quantize_1x128 applied to torch's GELU output.
+ */
+int ltxfp8_gelu_tanh_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld,
+                                    float* sfa, int64_t sfa_ld, int flags, void* stream);
+
+/*
  * RMSNorm + interleaved RoPE for attention q/k: per row of x bf16 [rows, dim]
  * (dim % 8 == 0, dim <= 8192), v = x * (rsqrt(sum(x^2) * (1/dim)) * w) (no epsilon;
  * weights bf16 [dim] or NULL for none), then for each pair (2i, 2i+1)

@@ -32,6 +32,7 @@
 //               (kind::f16) over [x A^T | B], promoted with scale alpha.
 #pragma once
 
+#include "gelu.cuh"
 #include "ptx.cuh"
 
 namespace ltxfp8 {
@@ -48,8 +49,9 @@ constexpr int kGemmThreads = 384;
 constexpr uint32_t kTmemCols = 512;                   // 2 x 256 fp32 accumulator columns
 constexpr int kLoraChunk = 64;                        // bf16 K elements per LoRA block (128 B rows)
 constexpr uint32_t kStagingAmaxBytes = 2 * kBM * 4;  // abs-max per (128-column half, row)
-constexpr uint32_t kGemmSmemBytes =
-    kStages * kStageBytes + kStagingBytes + kStagingAmaxBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kGemmBarrierBytes = 256;
+constexpr uint32_t kGemmSmemBytes = kStages * kStageBytes + kStagingBytes + kStagingAmaxBytes + 1024 /*align*/ +
+                                    kGemmBarrierBytes + kGeluTabBytes;
 
 // Register split between the producer/MMA warpgroup and the two epilogue
 // warpgroups; the launch must provide kGemmThreads * kGemmLaunchRegs.
@@ -65,13 +67,6 @@ enum GemmFlags : int {
   kGemmGeluFast = 8,        // GELU as x / (1 + 2^a) with approximate instructions (else torch's formula)
   kGemmRequantTriton = 16,  // requantisation scales as the Triton quantiser computes them (div.full)
 };
-
-// bf16 GELU of a bf16 value held in fp32 (exact), rounded to bf16: torch's formula or
-// the fast form, chosen per launch (warp-uniform).
-__device__ __forceinline__ float2 gemm_gelu2(float2 x, bool fast) {
-  if (fast) return gelu_tanh_f32x2(x);
-  return make_float2(gelu_tanh_torch(x.x), gelu_tanh_torch(x.y));
-}
 
 // Scale pair of a requantised 1x128 group from its abs-max: the Triton quantiser's
 // divisions (triton_ops.py:19-21) or torch's reciprocal-multiply (functional.py:142-144).
@@ -164,6 +159,27 @@ __device__ __forceinline__ uint32_t gemm_staging_off(int r, int chunk) {
          static_cast<uint32_t>(((chunk & 7) ^ (r & 7)) * 16);
 }
 
+// The staged tile's second pass: GELU (in place) and the 1x128 group abs-max of one
+// 8-column chunk (`chunk`, counted across the tile) of this thread's row.  The pass
+// over a tile runs one chunk per K block of the next tile, while the tensor core
+// works, instead of between the tiles where the MMA would wait for the TMEM buffers.
+template <bool kGelu, bool kRequant>
+__device__ __forceinline__ void staged_post_chunk(uint8_t* staging, int r_local, int chunk, bool gelu_fast,
+                                                  const uint16_t* gelu_tab, float& gmax) {
+  uint4* ptr = reinterpret_cast<uint4*>(staging + gemm_staging_off(r_local, chunk));
+  const uint4 v = *ptr;
+  uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+  if constexpr (kGelu) {
+    gelu_bf16x8_inplace(w4, gelu_fast, gelu_tab);
+    *ptr = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+  if constexpr (kRequant) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      gmax = fmax_nan(gmax, fmax_nan(fabsf(__uint_as_float(w4[i] << 16)), fabsf(__uint_as_float(w4[i] & 0xFFFF0000u))));
+  }
+}
+
 // Fold one K block's raw partial sums (TMEM buffer `it & 1`) into the fp32
 // accumulators of this thread's row: acc += scale * partial, 128 columns as 64
 // packed f32x2 FMAs.  Releases the TMEM buffer as soon as it has been read.
@@ -217,10 +233,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* stg_empty = stg_full + 1;  // [1] store warps -> promotion warps
   uint64_t* drain = stg_empty + 1;     // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(staging + kStagingBytes + kStagingAmaxBytes + kGemmBarrierBytes);
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
   const int lane = static_cast<int>(lane_id());
 
+  if (kGelu && !(p.flags & kGemmGeluFast)) gelu_table_fill(gelu_tab, static_cast<int>(threadIdx.x), kGemmThreads);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -437,6 +455,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t tcount = 0;              // staged tiles so far (staging barrier phases)
     bool ok = true;
     const int total_units = p.total_tiles * p.k_splits;
+    // Second pass over the staged tile (GELU / requant abs-max), deferred: post_c is
+    // the next chunk of it to process, 16 when none is pending.
+    constexpr bool kPost = kGelu || kRequant;
+    const bool gelu_fast = (p.flags & kGemmGeluFast) != 0;
+    const int r_local = sp * 32 + lane;
+    int post_c = 16;
+    float gmax = 0.0f;  // abs-max of this thread's 1x128 group of the staged tile
+    auto post_step = [&]() {
+      staged_post_chunk<kGelu, kRequant>(staging, r_local, half * 16 + post_c, gelu_fast, gelu_tab, gmax);
+      if (++post_c == 16) {
+        if constexpr (kRequant) stg_amax[half * kBM + r_local] = gmax;
+        fence_proxy_async_smem();  // the store warps hand these bytes straight to TMA
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stg_full);
+      }
+    };
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       const GemmUnit w = gemm_unit(u, p);
       const int row = w.mt * kBM + sp * 32 + lane;
@@ -472,6 +506,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             sb[j] = (col_ok && kn < w.n_fp8) ? __ldg(sfb_blk + kn) : 0.f;
             ok = promote_kblock(tfull, tempty, tmem_base, sp, half, it, scale, lane, acc);
             ++it;
+            if constexpr (kPost) {
+              if (post_c < 16 && ok) post_step();
+            }
           }
         }
       }
@@ -501,15 +538,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       // bf16(acc + bias) into the staging tile once the store warps have drained
       // the previous one.  Every promotion warp arrives once per tile, in range or not.
+      if constexpr (kPost) {
+        while (post_c < 16) post_step();  // the previous tile's pass, if the K loop was too short
+      }
       if (!__all_sync(0xffffffffu, mbar_wait(stg_empty, (tcount & 1u) ^ 1u, kStStagingEmpty))) {
         ok = false;
         break;
       }
       const bool has_bias = (p.flags & kGemmBias) != 0 && col_ok;
-      const bool gelu_fast = (p.flags & kGemmGeluFast) != 0;
       const float4* bias4 = reinterpret_cast<const float4*>(p.bias + col0);
-      const int r_local = sp * 32 + lane;
-      float gmax = 0.0f;  // abs-max of this thread's 1x128 group (requant)
 #pragma unroll
       for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 columns
         float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
@@ -518,32 +555,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           b1 = __ldg(bias4 + 2 * c + 1);
         }
         const float2 a0 = acc[4 * c], a1 = acc[4 * c + 1], a2 = acc[4 * c + 2], a3 = acc[4 * c + 3];
-        uint32_t w4[4] = {pack_bf16x2(a0.x + b0.x, a0.y + b0.y), pack_bf16x2(a1.x + b0.z, a1.y + b0.w),
-                          pack_bf16x2(a2.x + b1.x, a2.y + b1.y), pack_bf16x2(a3.x + b1.z, a3.y + b1.w)};
-        if constexpr (kGelu) {
-          // The reference applies GELU to the bf16 tensor bf16(acc + bias) and
-          // rounds the result to bf16.
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 y = gemm_gelu2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)),
-                                        gelu_fast);
-            w4[i] = pack_bf16x2(y.x, y.y);
-          }
-        }
-        if constexpr (kRequant) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            gmax = fmax_nan(gmax, fmax_nan(fabsf(__uint_as_float(w4[i] << 16)),
-                                           fabsf(__uint_as_float(w4[i] & 0xFFFF0000u))));
-        }
+        // The reference applies GELU to the bf16 tensor bf16(acc + bias) and rounds
+        // the result to bf16: the second pass reads these values back.
         *reinterpret_cast<uint4*>(staging + gemm_staging_off(r_local, half * 16 + c)) =
-            make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            make_uint4(pack_bf16x2(a0.x + b0.x, a0.y + b0.y), pack_bf16x2(a1.x + b0.z, a1.y + b0.w),
+                       pack_bf16x2(a2.x + b1.x, a2.y + b1.y), pack_bf16x2(a3.x + b1.z, a3.y + b1.w));
       }
-      if constexpr (kRequant) stg_amax[half * kBM + r_local] = gmax;
-      fence_proxy_async_smem();  // the store warps may hand these bytes straight to TMA
-      __syncwarp();
-      if (lane == 0) mbar_arrive(stg_full);
+      if constexpr (kPost) {
+        post_c = 0;
+        gmax = 0.0f;
+      } else {
+        fence_proxy_async_smem();  // the store warps hand these bytes straight to TMA
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stg_full);
+      }
       ++tcount;
+    }
+    if constexpr (kPost) {
+      if (ok)
+        while (post_c < 16) post_step();  // the last tile's pass
     }
   }
 

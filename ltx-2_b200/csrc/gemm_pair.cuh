@@ -45,8 +45,9 @@ constexpr int kScaleRing = 4;  // K blocks of scales in flight per promotion thr
 // warp's 32 lanes read 32 consecutive words.
 constexpr uint32_t kScaleRingBytes = 256 * kScaleRing * 2 * 4;
 constexpr uint32_t kStagingAmaxBytes = 2 * kRowsPerCta * 4;  // abs-max per (128-column half, row)
+constexpr uint32_t kBarrierBytes = 256;
 constexpr uint32_t kSmemBytes =
-    kStages * kStageBytes + kStagingBytes + kStagingAmaxBytes + kScaleRingBytes + 1024 + 256;
+    kStages * kStageBytes + kStagingBytes + kStagingAmaxBytes + kScaleRingBytes + 1024 + kBarrierBytes + kGeluTabBytes;
 
 constexpr uint32_t kRegsCtrl = 40;   // warps 0-3: producer, MMA, store warps
 constexpr uint32_t kRegsEpi = 232;   // warps 4-11: promotion
@@ -122,10 +123,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* stg_empty = stg_full + 1; // [1]
   uint64_t* drain = stg_empty + 1;    // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(scale_ring + kScaleRingBytes + kBarrierBytes);
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
   const int lane = static_cast<int>(lane_id());
   const uint32_t rank = cluster_ctarank();
+  if (kGelu && !(p.flags & kGemmGeluFast)) gelu_table_fill(gelu_tab, static_cast<int>(threadIdx.x), kThreads);
   const bool leader = rank == 0;
   const int cluster_id = static_cast<int>(blockIdx.x) >> 1;
   const int num_clusters = static_cast<int>(gridDim.x) >> 1;
@@ -405,12 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w4[4] = {pack_bf16x2(a0.x + b0.x, a0.y + b0.y), pack_bf16x2(a1.x + b0.z, a1.y + b0.w),
                           pack_bf16x2(a2.x + b1.x, a2.y + b1.y), pack_bf16x2(a3.x + b1.z, a3.y + b1.w)};
         if constexpr (kGelu) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 y = gemm_gelu2(make_float2(__uint_as_float(w4[i] << 16), __uint_as_float(w4[i] & 0xFFFF0000u)),
-                                        gelu_fast);
-            w4[i] = pack_bf16x2(y.x, y.y);
-          }
+          gelu_bf16x8_inplace(w4, gelu_fast, gelu_tab);
         }
         if constexpr (kRequant) {
 #pragma unroll

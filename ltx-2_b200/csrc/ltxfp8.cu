@@ -762,6 +762,44 @@ int ltxfp8_gelu_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld
   return LTXFP8_OK;
 }
 
+int ltxfp8_gelu_tanh_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t x_ld, void* q, int64_t q_ld,
+                                    float* sfa, int64_t sfa_ld, int flags, void* stream) {
+  if (M < 0 || K <= 0 || K % 128 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "gelu_tanh_quantize: need K %% 128 == 0, K > 0, M >= 0 (M=%lld K=%lld)", (long long)M, (long long)K);
+  if (flags != LTXFP8_QUANT_TORCH && flags != LTXFP8_QUANT_TRITON) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gelu_tanh_quantize: unknown mode %d", flags);
+  if (M == 0) return LTXFP8_OK;
+  if (!x || !q || !sfa) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gelu_tanh_quantize: null pointer");
+  if (x_ld < K || q_ld < K || sfa_ld < M) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gelu_tanh_quantize: leading dimension too small");
+  if (!aligned(x, 16) || x_ld % 8 != 0) return fail(LTXFP8_ERR_MISALIGNED, "gelu_tanh_quantize: x must be 16-byte aligned with x_ld %% 8 == 0");
+  if (!aligned(q, 8) || q_ld % 8 != 0) return fail(LTXFP8_ERR_MISALIGNED, "gelu_tanh_quantize: q must be 8-byte aligned with q_ld %% 8 == 0");
+  if (!aligned(sfa, 4)) return fail(LTXFP8_ERR_MISALIGNED, "gelu_tanh_quantize: sfa must be 4-byte aligned");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t KB = K / 128;
+  const int64_t units = ((M + kQuantRowsPerBlock - 1) / kQuantRowsPerBlock) *
+                        ((KB + kQuantGroupsPerThread - 1) / kQuantGroupsPerThread);
+  // Persistent grid, one wave: each CTA fills its GELU table once.
+  static std::atomic<int> per_sm{0};
+  if (per_sm.load() == 0) {
+    int n = 0;
+    cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gelu_tanh_quant_kernel<kQuantTriton>, 256, 0);
+    if (oe != cudaSuccess) return cuda_fail(oe, "gelu_tanh_quantize occupancy");
+    per_sm.store(n > 0 ? n : 1);
+  }
+  const int64_t cap = static_cast<int64_t>(d->sms) * per_sm.load();
+  const unsigned grid = static_cast<unsigned>(units < cap ? units : cap);
+  auto s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* qb = static_cast<uint8_t*>(q);
+  if (flags == LTXFP8_QUANT_TRITON)
+    gelu_tanh_quant_kernel<kQuantTriton><<<grid, 256, 0, s>>>(xb, x_ld, M, KB, qb, q_ld, sfa, sfa_ld);
+  else
+    gelu_tanh_quant_kernel<kQuantTorch><<<grid, 256, 0, s>>>(xb, x_ld, M, KB, qb, q_ld, sfa, sfa_ld);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gelu_tanh_quantize launch");
+  return LTXFP8_OK;
+}
+
 // One launch (plus its split-K reduction) of the GEMM over output rows
 // [row0, row0 + rows): the operands and outputs of those rows are addressed by
 // offsetting A, sfa, D, the requant outputs and the LoRA rows; N, K, W, sfb and

@@ -2,6 +2,7 @@
 // and the 1x128 dequantiser.  All three are HBM-bound streaming kernels.
 #pragma once
 
+#include "gelu.cuh"
 #include "ptx.cuh"
 
 namespace ltxfp8 {
@@ -85,6 +86,72 @@ __global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat1
     if (row_ok && kb < KB) {
       *reinterpret_cast<uint2*>(q + row * q_ld + kb * 128 + l16 * 8) = make_uint2(w[0], w[1]);
       if (l16 == 0) sfa[kb * sfa_ld + row] = inv;
+    }
+  }
+}
+
+// torch's GELU-tanh, then the 1x128 quantiser: the reference FFN's unfused chain
+// h = F.gelu(linear1(x), approximate="tanh") (bf16) followed by blockwise::quantize
+// (ltx-core/src/ltx_core/model/transformer/gelu_approx.py:10, ltx-kernels/.../linear.py:91-93),
+// from the up projection's bf16 output.  Codes and scales equal quant_act_1x128_kernel
+// applied to torch's bf16 GELU output.  A persistent grid: every CTA fills the 10.5 KB
+// GELU table once, then walks units of 16 rows x kQuantGroupsPerThread groups, groups
+// fastest (consecutive CTAs read consecutive bytes of the same rows).
+template <int kMode>
+__global__ void __launch_bounds__(256) gelu_tanh_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_ld,
+                                                              int64_t M, int64_t KB, uint8_t* __restrict__ q,
+                                                              int64_t q_ld, float* __restrict__ sfa,
+                                                              int64_t sfa_ld) {
+  __shared__ __align__(16) uint16_t tab[2 * kGeluTabWindow];
+  gelu_table_fill(tab, static_cast<int>(threadIdx.x), 256);
+  __syncthreads();
+  const int t = threadIdx.x;
+  const int l16 = t & 15;
+  const int64_t row_blocks = (M + kQuantRowsPerBlock - 1) / kQuantRowsPerBlock;
+  const int64_t kb_blocks = (KB + kQuantGroupsPerThread - 1) / kQuantGroupsPerThread;
+  const int64_t units = row_blocks * kb_blocks;
+  for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    const int64_t rb = unit / kb_blocks, kbb = unit - rb * kb_blocks;
+    const int64_t row = rb * kQuantRowsPerBlock + (t >> 4);
+    const int64_t kb0 = kbb * kQuantGroupsPerThread;
+    const bool row_ok = row < M;
+    uint4 v[kQuantGroupsPerThread];
+#pragma unroll
+    for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+      const int64_t kb = kb0 + u;
+      v[u] = (row_ok && kb < KB) ? __ldg(reinterpret_cast<const uint4*>(x + row * x_ld + kb * 128 + l16 * 8))
+                                 : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+      const int64_t kb = kb0 + u;
+      const uint4 g = gelu_bf16x8(v[u], smem_u32(tab));
+      float f[8];
+      bf16x8_to_f32(g, f);
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = (kMode == kQuantTriton) ? fmaxf(amax, fabsf(f[i])) : fmax_nan(amax, fabsf(f[i]));
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, amax, off, 16);
+        amax = (kMode == kQuantTriton) ? fmaxf(amax, o) : fmax_nan(amax, o);
+      }
+      float s, inv;
+      group_scale<kMode>(amax, s, inv);
+      const bool in_range = (kMode == kQuantTriton) || isfinite(s);
+      uint32_t w[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float v0 = __fmul_rn(f[4 * i], s), v1 = __fmul_rn(f[4 * i + 1], s);
+        const float v2 = __fmul_rn(f[4 * i + 2], s), v3 = __fmul_rn(f[4 * i + 3], s);
+        const uint16_t lo = in_range ? f32x2_to_e4m3x2_inrange(v0, v1) : f32x2_to_e4m3x2(v0, v1);
+        const uint16_t hi = in_range ? f32x2_to_e4m3x2_inrange(v2, v3) : f32x2_to_e4m3x2(v2, v3);
+        w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+      if (row_ok && kb < KB) {
+        *reinterpret_cast<uint2*>(q + row * q_ld + kb * 128 + l16 * 8) = make_uint2(w[0], w[1]);
+        if (l16 == 0) sfa[kb * sfa_ld + row] = inv;
+      }
     }
   }
 }

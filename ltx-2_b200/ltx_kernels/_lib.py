@@ -89,6 +89,7 @@ SIGNATURES = {
     "ltxfp8_rms_fma": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),
     "ltxfp8_gated_attention": (_i32, [_vp, _vp, _i32, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),
     "ltxfp8_gelu_quantize_1x128": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i32, _vp]),
+    "ltxfp8_gelu_tanh_quantize_1x128": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i32, _vp]),
     "ltxfp8_rms_norm_rope": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i32, _vp]),
     "ltxfp8_rms_norm_split_rope": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
                                           _vp, _vp, _i32, _vp]),

@@ -278,6 +278,26 @@ def gelu_quantize_1x128(x: torch.Tensor, mode: int = L.QUANT_TORCH) -> Tuple[tor
     return q, s
 
 
+def gelu_tanh_quantize_1x128(x: torch.Tensor, mode: int = L.QUANT_TORCH) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [..., K] -> 1x128 quant of torch's ``F.gelu(x, approximate="tanh")`` (bf16):
+    (e4m3 [M, K], scales).  The reference FFN's GELU followed by the down projection's
+    input quantisation (gelu_approx.py:10, linear.py:91-93), in one pass over x."""
+    _require_cuda("gelu_tanh_quantize_1x128", x)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"gelu_tanh_quantize_1x128 expects bf16 input, got {x.dtype}")
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    s = empty_act_scales(M, K // 128 if K % 128 == 0 else 0, x.device)
+    with _DeviceGuard(x):
+        L.check(L.load().ltxfp8_gelu_tanh_quantize_1x128(x2.data_ptr(), M, K, x2.stride(0), q.data_ptr(), K,
+                                                          s.data_ptr(), align4(M), mode, _stream(x)))
+    return q, s
+
+
 def rms_norm_rope(x: torch.Tensor, cos_freqs: torch.Tensor, sin_freqs: torch.Tensor,
                   weights: Optional[torch.Tensor] = None, out_fp8: bool = False) -> torch.Tensor:
     """RMSNorm + interleaved RoPE over the last dim of bf16 x; cos/sin reshape to (rows, dim)."""

@@ -137,3 +137,29 @@ def test_dequant_weight_layout_via_fuse_helper(cuda_device):
     out = F.blockwise_dequantize((q.unsqueeze(0), rows)).view(256, 384)
     ref = O.dequant_1x128(bits(q), rows.cpu().numpy(), rows.shape[1], 1)
     assert np.array_equal(bits(out), ref)
+
+
+@pytest.mark.parametrize("M,K", [(512, 128), (37, 640), (1000, 2048)])
+def test_gelu_tanh_quant_equals_torch_gelu_then_quant(cuda_device, M, K):
+    """The FFN's GELU + requant in one pass equals torch's CUDA F.gelu(approximate="tanh")
+    followed by the 1x128 quantiser, codes and scales bit for bit, in both arithmetics;
+    (512, 128) holds every bf16 bit pattern once."""
+    import torch.nn.functional as F
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import ops
+    if (M, K) == (512, 128):
+        x = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).reshape(M, K).to(cuda_device)
+    else:
+        x = (activations(M, K, seed=M + K) * 4.0).to(torch.bfloat16).to(cuda_device)
+        x[0, :128] = 0.0
+        x[min(1, M - 1), 128:256] = 1e-30
+    y = F.gelu(x, approximate="tanh")
+    for mode in (L.QUANT_TORCH, L.QUANT_TRITON):
+        q, s = ops.gelu_tanh_quantize_1x128(x, mode)
+        rq, rs = ops.quantize_1x128(y, mode)
+        torch.cuda.synchronize()
+        a, b = q.view(torch.uint8), rq.view(torch.uint8)
+        same = (a == b) | (((a & 0x7F) == 0x7F) & ((b & 0x7F) == 0x7F))
+        assert bool(same.all()), (mode, int((~same).sum()))
+        sv, rv = s.view(torch.int32), rs.view(torch.int32)
+        assert bool(((sv == rv) | (torch.isnan(s) & torch.isnan(rs))).all()), mode
