@@ -1134,19 +1134,24 @@ def run_producers(args, rank: int, world: int, local: int):
     logits = (torch.randn(B, S, heads, generator=g, device=dev) * 3).to(torch.bfloat16)
     names = list(nbytes)
 
-    def step(ev=None):
+    from ltx_kernels import _lib as L
+
+    def step(ev=None, mode=None):
+        # the reference's GPU arithmetic (triton mode) unless told otherwise: the default
+        # of the reference-named ops
+        mode = L.QUANT_TRITON if mode is None else mode
         if ev:
             ev[0].record()
-        ops.adanorm_quantize(x, sc, sh)
+        ops.adanorm_quantize(x, sc, sh, mode)
         if ev:
             ev[1].record()
-        ops.rms_fma(x, y, z, True)
+        ops.rms_fma(x, y, z, True, mode)
         if ev:
             ev[2].record()
-        ops.gated_attention(y, logits, True)
+        ops.gated_attention(y, logits, True, mode)
         if ev:
             ev[3].record()
-        ops.gelu_quantize_1x128(y)
+        ops.gelu_quantize_1x128(y, mode)
         if ev:
             ev[4].record()
 
@@ -1171,6 +1176,16 @@ def run_producers(args, rank: int, world: int, local: int):
     elapsed = t0.elapsed_time(t1)
     per_kernel = [sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps)) / args.steps
                   for j in range(4)]
+    # the same launches in IEEE arithmetic (torch mode), reported beside
+    for _ in range(2):
+        step(mode=L.QUANT_TORCH)
+    barrier()
+    evt = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        step(evt[i], L.QUANT_TORCH)
+    barrier()
+    per_kernel_torch = [sum(evt[i][j].elapsed_time(evt[i][j + 1]) for i in range(args.steps)) / args.steps
+                        for j in range(4)]
 
     # end to end through the reference-named ops: x, y from pinned host memory, codes back
     x_host, y_host = x.cpu().pin_memory(), y.cpu().pin_memory()
@@ -1238,6 +1253,9 @@ def run_producers(args, rank: int, world: int, local: int):
                        "parallelism": f"token-sharded dp{world}", "l2": "working set > L2 (x, y 403 MB each); no flush"},
             "kernels_ms": {n: round(t, 4) for n, t in zip(names, per_kernel)},
             "kernels_gbs": {n: round(nbytes[n] / (t * 1e-3) / 1e9, 1) for n, t in zip(names, per_kernel)},
+            "arithmetic": "triton mode (the reference's GPU arithmetic); torch mode in kernels_ms_torch_mode",
+            "kernels_ms_torch_mode": {n: round(t, 4) for n, t in zip(names, per_kernel_torch)},
+            "kernels_gbs_torch_mode": {n: round(nbytes[n] / (t * 1e-3) / 1e9, 1) for n, t in zip(names, per_kernel_torch)},
             "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic},
             "cpu_baseline": cpu,
