@@ -3,9 +3,12 @@
 * ``fp8_linear`` -- one call for quantise (if bf16) + GEMM + epilogue
   (bias, GELU-tanh, 1x128 requantisation, runtime LoRA).
 * ``BlockwiseFP8FeedForward`` -- the DiT FFN (ltx-core/src/ltx_core/model/
-  transformer/feed_forward.py:6-15: Linear(d, 4d) -> GELU-tanh -> Linear(4d, d))
-  with the GELU and the down projection's input quantisation folded into the
-  up projection's epilogue, so the 4d-wide hidden state never exists in bf16.
+  transformer/feed_forward.py:6-15: Linear(d, 4d) -> GELU-tanh -> Linear(4d, d)):
+  the up projection writes bf16 ``h``, one streaming pass applies torch's GELU and
+  quantises it for the down projection (``ops.gelu_tanh_quantize_1x128``).  The GEMM
+  epilogue can do the same in-kernel (``fused_epilogue=True``, no bf16 hidden state),
+  with identical codes and scales, but the GEMM's epilogue warps are on its critical
+  path, so the separate pass is faster at every measured size (3-16 %).
 * ``BlockwiseFP8LoRALinear`` -- ``W x + alpha B (A x)`` at run time: the skinny
   ``A x`` GEMM runs first, ``B (A x)`` is folded into the FP8 GEMM as extra bf16
   K blocks.  The reference instead merges LoRA into the weights at load time
@@ -67,13 +70,17 @@ def fp8_linear(x: Activation, weight: torch.Tensor, weight_scale: torch.Tensor, 
 
 
 class BlockwiseFP8FeedForward(nn.Module):
-    """FFN with the GELU and the hidden-state requantisation fused into the up projection."""
+    """FFN: up projection, torch's GELU-tanh + 1x128 requantisation of the hidden state,
+    down projection.  ``fused_epilogue``: GELU and requant inside the up projection's
+    GEMM epilogue instead of a separate streaming pass (same results)."""
 
-    def __init__(self, dim: int, dim_out: int, mult: int = 4, bias: bool = True, device=None):
+    def __init__(self, dim: int, dim_out: int, mult: int = 4, bias: bool = True, device=None,
+                 fused_epilogue: bool = False):
         super().__init__()
         inner = int(dim * mult)
         self.proj_in = BlockwiseFP8Linear(dim, inner, bias=bias, device=device)
         self.proj_out = BlockwiseFP8Linear(inner, dim_out, bias=bias, device=device)
+        self.fused_epilogue = fused_epilogue
 
     @classmethod
     def from_linears(cls, up: BlockwiseFP8Linear, down: BlockwiseFP8Linear) -> "BlockwiseFP8FeedForward":
@@ -81,11 +88,17 @@ class BlockwiseFP8FeedForward(nn.Module):
         nn.Module.__init__(ff)
         ff.proj_in = up
         ff.proj_out = down
+        ff.fused_epilogue = False
         return ff
 
     def forward(self, x: Activation) -> torch.Tensor:
-        _, hq, hs = fp8_linear(x, self.proj_in.weight, self.proj_in.weight_scale, self.proj_in.bias,
-                               gelu=True, requant=True, write_d=False)
+        if self.fused_epilogue:
+            _, hq, hs = fp8_linear(x, self.proj_in.weight, self.proj_in.weight_scale, self.proj_in.bias,
+                                   gelu=True, requant=True, write_d=False)
+        else:
+            h = fp8_linear(x, self.proj_in.weight, self.proj_in.weight_scale, self.proj_in.bias)
+            hq, hs = ops.gelu_tanh_quantize_1x128(h, quant_mode_code())
+            hq = hq.view(*h.shape)
         return fp8_linear((hq, hs), self.proj_out.weight, self.proj_out.weight_scale, self.proj_out.bias)
 
 
