@@ -109,3 +109,36 @@ def test_stream_with_split_k_chunks(cuda_device):
         torch.cuda.synchronize()
     diff = (out.float() - ref).abs().max().item()
     assert diff <= 0.02 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("rows", [300, 2048])
+def test_ffn_module_paths_agree(cuda_device, rows):
+    """BlockwiseFP8FeedForward: the default path (up projection to bf16, then one GELU +
+    requant pass) and the fused-epilogue path give identical outputs, in both
+    arithmetics; and both equal the reference's unfused chain written with torch's GELU."""
+    import torch.nn.functional as Fn
+    from ltx_kernels import _lib as L
+    from ltx_kernels.blockwise import BlockwiseFP8FeedForward, ops
+    import ltx_kernels.blockwise.functional as F
+    D, H = 512, 2048
+    up, down = _linear(D, H, cuda_device, 11), _linear(H, D, cuda_device, 12)
+    ff = BlockwiseFP8FeedForward.from_linears(up, down)
+    x = activations(rows, D, seed=rows + 5).to(cuda_device)
+    before = F.get_quant_mode()
+    try:
+        for mode in ("triton", "torch"):
+            F.set_quant_mode(mode)
+            ff.fused_epilogue = False
+            y_split = ff(x)
+            ff.fused_epilogue = True
+            y_fused = ff(x)
+            code = L.QUANT_TRITON if mode == "triton" else L.QUANT_TORCH
+            q, s = ops.quantize_1x128(x, code)
+            h = Fn.gelu(ops.gemm(q, s, up.weight, up.weight_scale, up.bias), approximate="tanh")
+            hq, hs = ops.quantize_1x128(h, code)
+            y_chain = ops.gemm(hq, hs, down.weight, down.weight_scale, down.bias)
+            torch.cuda.synchronize()
+            assert torch.equal(y_split, y_fused), mode
+            assert torch.equal(y_split.reshape(rows, D), y_chain), mode
+    finally:
+        F.set_quant_mode(before)
