@@ -85,7 +85,8 @@ def test_fused_gelu_requant_vs_torch_gelu_config1(cuda_device):
     linear.py:91-93).  Here the fused epilogue's bf16 GELU and its 1x128 requant are
     compared with exactly that chain run on the kernel's own bf16 pre-activation
     bf16(acc + bias) (the same accumulation), over the whole config-1 tensor:
-    * default GELU + triton-mode requant: identical, every value and every group;
+    * default GELU + triton-mode requant: identical, every value and every group (and
+      so is the separate GELU + requant pass the FFN module uses);
     * the fast GELU form: the fractions of GELU values and requant groups that differ
       are reported and bounded."""
     import torch.nn.functional as Fn
@@ -99,7 +100,10 @@ def test_fused_gelu_requant_vs_torch_gelu_config1(cuda_device):
     pre = ops.gemm(aq, asc, w1q, w1s, b1)                                   # bf16(acc + bias)
     tg = Fn.gelu(pre, approximate="tanh")                                   # the reference's GELU
     tq, ts = ops.quantize_1x128(tg, L.QUANT_TRITON)                         # the reference's quantiser
-    del pre
+    # the FFN module's default path: one streaming GELU + requant pass over bf16(acc + bias)
+    gq, gs = ops.gelu_tanh_quantize_1x128(pre, L.QUANT_TRITON)
+    assert torch.equal(gq.view(torch.uint8), tq.view(torch.uint8)) and torch.equal(gs, ts)
+    del pre, gq, gs
     ordered = lambda t: torch.where(t < 0, -(t.to(torch.int32) & 0x7FFF), t.to(torch.int32))
     for gelu, limits in ((True, (0.0, 0.0)), ("fast", (0.08, 0.02))):
         h, hq, hs = ops.gemm(aq, asc, w1q, w1s, b1, gelu=gelu, requant=True, write_d=True,
