@@ -398,6 +398,11 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
         d = None
     else:
         d = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a_q.device)
+    if M == 0:  # no tokens: empty results, nothing to launch (the C ABI takes M >= 1)
+        if requant:
+            return d, torch.empty((0, N), dtype=torch.float8_e4m3fn, device=a_q.device), \
+                empty_act_scales(0, N // 128, a_q.device)
+        return d
     ep = L.Epilogue()
     if gelu == "fast":
         ep.gelu_tanh = L.GELU_TANH_FAST

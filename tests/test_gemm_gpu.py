@@ -437,3 +437,27 @@ def test_gemm_rejects_bad_out(cuda_device):
                 torch.empty(M, N, dtype=torch.bfloat16)):
         with pytest.raises(RuntimeError):
             ops.gemm(aq, asc, wq, wsc, b, out=bad)
+
+
+def test_gemm_empty_token_batch(cuda_device):
+    """No tokens: empty results with the right shapes and nothing launched (the C ABI
+    takes M >= 1), through ops.gemm and the layer modules."""
+    from ltx_kernels.blockwise import BlockwiseFP8FeedForward, BlockwiseFP8Linear, ops
+    K, N = 256, 384
+    x = torch.empty((0, K), dtype=torch.bfloat16, device=cuda_device)
+    aq, asc = ops.quantize_1x128(x)
+    wq, wsc = ops.quantize_weight_128x128(weights(N, K, seed=5).to(cuda_device))
+    b = make_bias(N).to(cuda_device)
+    d = ops.gemm(aq, asc, wq, wsc, b)
+    assert tuple(d.shape) == (0, N) and d.dtype == torch.bfloat16
+    d2, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True)
+    assert tuple(d2.shape) == (0, N) and tuple(q.shape) == (0, N) and tuple(s.shape) == (0, N // 128)
+    lin = BlockwiseFP8Linear(K, N, device=cuda_device)
+    lin.weight.data, lin.weight_scale.data, lin.bias.data = wq, wsc, b
+    assert tuple(lin(x.view(1, 0, K)).shape) == (1, 0, N)
+    down = BlockwiseFP8Linear(N, K, device=cuda_device)
+    down.weight.data, down.weight_scale.data = ops.quantize_weight_128x128(weights(K, N, seed=6).to(cuda_device))
+    ff = BlockwiseFP8FeedForward.from_linears(lin, down)
+    assert tuple(ff(x).shape) == (0, K)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
