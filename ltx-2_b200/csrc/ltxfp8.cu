@@ -777,7 +777,7 @@ int ltxfp8_gelu_tanh_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t
   if (rc) return rc;
   const int64_t KB = K / 128;
   const int64_t units = ((M + kQuantRowsPerBlock - 1) / kQuantRowsPerBlock) *
-                        ((KB + kQuantGroupsPerThread - 1) / kQuantGroupsPerThread);
+                        ((KB + kGeluQuantGroups - 1) / kGeluQuantGroups);
   // Persistent grid, one wave: each CTA fills its GELU table once.
   static std::atomic<int> per_sm{0};
   if (per_sm.load() == 0) {

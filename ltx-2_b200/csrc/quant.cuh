@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(256) quant_act_1x128_kernel(const __nv_bfloat1
 // applied to torch's bf16 GELU output.  A persistent grid: every CTA fills the 10.5 KB
 // GELU table once, then walks units of 16 rows x kQuantGroupsPerThread groups, groups
 // fastest (consecutive CTAs read consecutive bytes of the same rows).
+constexpr int kGeluQuantGroups = 4;  // 1x128 groups per thread and unit
+
 template <int kMode>
 __global__ void __launch_bounds__(256) gelu_tanh_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_ld,
                                                               int64_t M, int64_t KB, uint8_t* __restrict__ q,
@@ -108,22 +110,22 @@ __global__ void __launch_bounds__(256) gelu_tanh_quant_kernel(const __nv_bfloat1
   const int t = threadIdx.x;
   const int l16 = t & 15;
   const int64_t row_blocks = (M + kQuantRowsPerBlock - 1) / kQuantRowsPerBlock;
-  const int64_t kb_blocks = (KB + kQuantGroupsPerThread - 1) / kQuantGroupsPerThread;
+  const int64_t kb_blocks = (KB + kGeluQuantGroups - 1) / kGeluQuantGroups;
   const int64_t units = row_blocks * kb_blocks;
   for (int64_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
     const int64_t rb = unit / kb_blocks, kbb = unit - rb * kb_blocks;
     const int64_t row = rb * kQuantRowsPerBlock + (t >> 4);
-    const int64_t kb0 = kbb * kQuantGroupsPerThread;
+    const int64_t kb0 = kbb * kGeluQuantGroups;
     const bool row_ok = row < M;
-    uint4 v[kQuantGroupsPerThread];
+    uint4 v[kGeluQuantGroups];
 #pragma unroll
-    for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+    for (int u = 0; u < kGeluQuantGroups; ++u) {
       const int64_t kb = kb0 + u;
       v[u] = (row_ok && kb < KB) ? __ldg(reinterpret_cast<const uint4*>(x + row * x_ld + kb * 128 + l16 * 8))
                                  : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kQuantGroupsPerThread; ++u) {
+    for (int u = 0; u < kGeluQuantGroups; ++u) {
       const int64_t kb = kb0 + u;
       const uint4 g = gelu_bf16x8(v[u], smem_u32(tab));
       float f[8];
