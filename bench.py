@@ -22,7 +22,7 @@ its SM89 mma.sync GEMM with fp32 accumulation, built from the reference's source
 into oracle/_ref) on config 0, config 1 and the headline GEMM, beside ours.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload dit_step|ffn|linear|qkv_lora|producers|sweep]
+                    [--workload dit_step|ffn|linear|qkv_lora|producers|sweep|fp6]
                     [--impl ours|reference] [--e2e-chunk T] [--m TOKENS]
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its token shard, no
@@ -1098,6 +1098,83 @@ def run_sweep(args, rank: int, world: int, local: int):
         "clocks": c}))
 
 
+# ----------------------------------------------------------------------------- FP6 weights
+FP6_SHAPES = [(128, 4096, 16384), (128, 16384, 4096), (1024, 4096, 4096), (8192, 4096, 16384),
+              (24576, 4096, 16384)]
+
+
+def run_fp6(args, rank: int, world: int, local: int):
+    """BlockwiseFP6Linear's GEMM (linear.py:212-250): the 6-bit weight streamed into the
+    tensor core (``gemm(..., w_fp6=True)``; with the tensor-core copy kept, and with the
+    per-call rewrite of the module's default) against unpack-to-e4m3 + FP8 GEMM (the
+    reference's algorithm, on this library's kernels and, when built, on the reference's
+    own ops_cpp unpack + SM89 GEMM), bias, bf16 out, each event-timed in isolation."""
+    import torch
+    from ltx_kernels.blockwise import ops
+    from oracle import refpath
+    if args.impl == "reference" or rank != 0:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the fp6 workload times GPU paths only; the "
+                              "reference's own GPU path is timed beside ours in the same line"}))
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    G = refpath.gemm() if refpath.available("gemm") else None
+    R = refpath.ops() if refpath.available("ops") else None
+    bw, bw_src = hbm_peak()
+    flush = L2Flush(dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    points, launches = [], 0
+    clk = ClockSampler(local).start()
+    for M, K, N in FP6_SHAPES:
+        w = torch.randn(N, K, generator=g, device=dev) * 0.02
+        wq, ws = ops.quantize_weight_128x128(w, scale_max=0.1172)
+        del w
+        b = (torch.randn(N, generator=g, device=dev) * 0.01).to(torch.bfloat16).float()
+        w6 = ops.fp6_pack(wq.view(torch.uint8))
+        tc, s6 = ops.fp6_to_tc(w6, ws)
+        aq, asc = ops.quantize_1x128(synth_acts(M, K, g, dev))
+        reps = 20 if M <= 2048 else 8
+        small = M * K + N * K + 2 * M * N < (126 << 20)
+        fl = flush if small else None
+        d6 = ops.gemm(aq, asc, tc, s6, b, w_fp6=True)
+        d8 = ops.gemm(aq, asc, ops.fp6_unpack(w6, K).view(torch.float8_e4m3fn), ws, b)
+        same = bool(torch.equal(d6, d8))
+        t_tc = time_launches(lambda: ops.gemm(aq, asc, tc, s6, b, w_fp6=True), reps, flush=fl)
+        t_tr = time_launches(lambda: ops.gemm(aq, asc, *ops.fp6_to_tc(w6, ws), b, w_fp6=True), reps, flush=fl)
+        t_un = time_launches(lambda: ops.gemm(aq, asc, ops.fp6_unpack(w6, K).view(torch.float8_e4m3fn), ws, b),
+                             reps, flush=fl)
+        t_f8 = time_launches(lambda: ops.gemm(aq, asc, wq, ws, b), reps, flush=fl)
+        launches += reps * (2 * ops.gemm_plan(M, N, K, dev)["launches"] + 2) * 2
+        by = M * K + 4 * M * K // 128 + N * K * 3 // 4 + 4 * (N // 128) * (K // 128) + 4 * N + 2 * M * N
+        p = {"M": M, "K": K, "N": N, "bit_identical_to_unpack_fp8": same,
+             "fp6_tc_us": t_tc * 1e3, "fp6_per_call_rewrite_us": t_tr * 1e3, "unpack_fp8_us": t_un * 1e3,
+             "fp8_weight_us": t_f8 * 1e3, "tflops_fp6_tc": 2.0 * M * N * K / t_tc / 1e9,
+             "alg_bytes_fp6": by, "gbs_fp6_tc": by / t_tc / 1e6, "hbm_frac_fp6_tc": by / t_tc / 1e6 / bw,
+             "speedup_tc_vs_unpack": t_un / t_tc, "speedup_rewrite_vs_unpack": t_un / t_tr}
+        if G is not None and R is not None:
+            def ref():
+                w8 = R.fp6_unpack(w6, K).view(torch.float8_e4m3fn)
+                d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                G.fp8_gemm_nt_sm89((aq, asc), (w8, ws), d, b, use_fast_accum=False)
+            p["ref_unpack_sm89_us"] = time_launches(ref, 5 if M <= 2048 else 3, warmup=1, flush=fl) * 1e3
+            p["speedup_tc_vs_ref"] = p["ref_unpack_sm89_us"] / p["fp6_tc_us"]
+        points.append(p)
+        del wq, ws, w6, tc, s6, aq, asc, d6, d8
+    c = clk.stop()
+    tot = sum(p["fp6_tc_us"] for p in points)
+    fl_tot = sum(2.0 * p["M"] * p["N"] * p["K"] for p in points)
+    print(json.dumps({
+        "metric": "blockwise FP6-weight GEMM TFLOP/s", "value": fl_tot / tot / 1e6, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": 1, "warmup": 3, "ms_per_step": tot / 1e3, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "e4m3 x e2m3 (6-bit) -> f32 accumulate, bf16 out",
+        "data": "synthetic (seeded; FP6-range weights from the 0.1172 quantiser)",
+        "config": {"workload": "BlockwiseFP6Linear GEMM shapes", "shapes": [list(x) for x in FP6_SHAPES],
+                   "l2": "flushed between launches when the working set fits in L2"},
+        "peaks": {"hbm_gbs": bw, "hbm_source": bw_src}, "points": points, "e2e": None, "cpu_baseline": None,
+        "gpu_launches": launches, "clocks": c}))
+
+
 # ----------------------------------------------------------------------------- producers
 PROD_B, PROD_S, PROD_H, PROD_HEADS = 2, 24576, 4096, 32   # config 3 video tokens (CFG batch 2), d = 4096
 
@@ -1315,7 +1392,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="dit_step",
-                    choices=["dit_step"] + sorted(WORKLOADS) + ["producers", "sweep"])
+                    choices=["dit_step"] + sorted(WORKLOADS) + ["producers", "sweep", "fp6"])
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="dit_step: strong (default) splits one step's tokens over the ranks, weak gives every "
                          "rank a full step")
@@ -1341,6 +1418,8 @@ def main():
         return run_producers(args, rank, world, local)
     if args.workload == "sweep":
         return run_sweep(args, rank, world, local)
+    if args.workload == "fp6":
+        return run_fp6(args, rank, world, local)
     return run_single(args, rank, world, local)
 
 

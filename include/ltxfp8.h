@@ -93,6 +93,17 @@ int ltxfp8_fp6_pack(const void* x, int64_t m, int64_t n, void* out, void* stream
 int ltxfp8_fp6_unpack(const void* x, int64_t m, int64_t n, void* out, void* stream);
 
 /*
+ * A packed FP6 weight w6 [N, K * 3 / 4] (ltxfp8_fp6_pack's layout) and its scales
+ * sfb [N/128, K/128] -> the operands of ltxfp8_gemm_fp6w: the same 6-bit codes in the
+ * tensor core's order (every 16 codes of a row in 12 bytes, code i at bits 6i..6i+5
+ * of their little-endian 96-bit word; w6_tc 32-byte aligned, same size as w6) and the
+ * scales x 2^-6 (a code read as e2m3 is 2^6 times the e4m3 value it stands for).
+ * N, K multiples of 128.
+ */
+int ltxfp8_fp6_to_tc(const void* w6, const float* sfb, int64_t N, int64_t K, void* w6_tc, float* sfb_tc,
+                     void* stream);
+
+/*
  * 1x128 dequantisation: out[m, k] = bf16(e4m3(q[m, k]) * scales[m * row_stride + (k/128) * col_stride]).
  * K % 128 == 0.  Replaces blockwise::dequantize
  * (ltx-kernels/src/ltx_kernels/blockwise/triton_ops.py:387-433).
@@ -239,6 +250,19 @@ typedef struct ltxfp8_epilogue {
 int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
                 const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
                 void* stream);
+
+/*
+ * ltxfp8_gemm with a 6-bit weight: W6 and sfb6 from ltxfp8_fp6_to_tc.  The weight
+ * streams from memory at 6 bits per element straight into the tensor core
+ * (kind::f8f6f4 with an e2m3 B operand), with no unpacked copy; the result is the
+ * same as ltxfp8_gemm on ltxfp8_fp6_unpack's e4m3 codes with the original scales.
+ * W6 32-byte aligned; every epilogue option is available.
+ * Replaces BlockwiseFP6Linear's fp8weight unpack followed by the FP8 GEMM
+ * (ltx-kernels/src/ltx_kernels/blockwise/linear.py:212-250, csrc/ops/fp6_pack.cu:112-211).
+ */
+int ltxfp8_gemm_fp6w(const void* A, const float* sfa, int64_t sfa_ld, const void* W6, const float* sfb6,
+                     const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
+                     void* stream);
 
 /*
  * Scratch bytes ltxfp8_gemm would use for split-K at this shape on the current

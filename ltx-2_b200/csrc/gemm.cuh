@@ -44,6 +44,11 @@ constexpr int kStages = 3;
 constexpr uint32_t kABytes = kBM * kBK;               // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK;               // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;   // 48 KB
+// W as packed 6-bit codes (kGemmWeightFp6): the TMA reads 96 B of each 128-code
+// row and writes them to shared memory as 16-code groups of 12 B with 4 B gaps
+// (the MMA's layout for 6-bit operands), so the B tile keeps its 128 B rows and
+// swizzle and only its transaction byte count changes.
+constexpr uint32_t kBBytesFp6 = kBBytes / 4 * 3;      // 24 KB
 constexpr uint32_t kStagingBytes = kBM * kBN * 2;     // 64 KB: bf16 [128, 256] epilogue tile
 constexpr int kGemmThreads = 384;
 constexpr uint32_t kTmemCols = 512;                   // 2 x 256 fp32 accumulator columns
@@ -66,6 +71,8 @@ enum GemmFlags : int {
   kGemmLora = 4,            // extra bf16 K blocks with scale lora_alpha
   kGemmGeluFast = 8,        // GELU as x / (1 + 2^a) with approximate instructions (else torch's formula)
   kGemmRequantTriton = 16,  // requantisation scales as the Triton quantiser computes them (div.full)
+  kGemmWeightFp6 = 32,      // W is e2m3 codes packed 6 bits each in the tensor core's order
+                            // (ltxfp8_fp6_to_tc), its scales already multiplied by 2^-6
 };
 
 // Scale pair of a requantised 1x128 group from its abs-max: the Triton quantiser's
@@ -284,6 +291,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       const int total_units = p.total_tiles * p.k_splits;
+      const uint32_t tx_fp8 = (p.flags & kGemmWeightFp6) ? kABytes + kBBytesFp6 : kStageBytes;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         const GemmUnit w = gemm_unit(u, p);
         const int m0 = w.mt * kBM, n0 = w.nt * kBN;
@@ -295,7 +303,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint8_t* sa = smem + s * kStageBytes;
           uint8_t* sb = sa + kABytes;
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          mbar_arrive_expect_tx(&full[s], kb < w.n_fp8 ? tx_fp8 : kStageBytes);
           if (kb < w.n_fp8) {
             tma_load_2d(&tmA, &full[s], sa, (w.kb_begin + kb) * kBK, m0);
             tma_load_2d(&tmB, &full[s], sb, (w.kb_begin + kb) * kBK, n0);
@@ -315,6 +323,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t kIdescF8 = make_idesc(0u, kBM, kBN);
       constexpr uint32_t kIdescBF16 = make_idesc(1u, kBM, kBN);
+      const uint32_t idesc_f8 = (p.flags & kGemmWeightFp6) ? with_b_format(kIdescF8, kFmtE2M3) : kIdescF8;
       uint32_t it = 0;
       bool ok = true;
       const int total_units = p.total_tiles * p.k_splits;
@@ -340,7 +349,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (kb < w.n_fp8) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)  // 4 x K32 (32 B of each 128 B row)
-              mma_f8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, kIdescF8, j > 0 ? 1u : 0u);
+              mma_f8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc_f8, j > 0 ? 1u : 0u);
           } else {
 #pragma unroll
             for (int j = 0; j < 4; ++j)  // 4 x K16 bf16 (32 B of each 128 B row)

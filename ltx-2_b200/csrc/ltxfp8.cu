@@ -522,6 +522,27 @@ int ltxfp8_fp6_unpack(const void* x, int64_t m, int64_t n, void* out, void* stre
   return fp6_launch(false, x, m, n, out, stream);
 }
 
+int ltxfp8_fp6_to_tc(const void* w6, const float* sfb, int64_t N, int64_t K, void* w6_tc, float* sfb_tc,
+                     void* stream) {
+  if (N <= 0 || K <= 0 || N % 128 != 0 || K % 128 != 0)
+    return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "fp6_to_tc: N and K must be positive multiples of 128");
+  if (!w6 || !sfb || !w6_tc || !sfb_tc) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "fp6_to_tc: null pointer");
+  if (!aligned(w6, 4) || !aligned(w6_tc, 32) || !aligned(sfb, 4) || !aligned(sfb_tc, 4))
+    return fail(LTXFP8_ERR_MISALIGNED, "fp6_to_tc: packed weight 4-byte, output 32-byte aligned");
+  DeviceInfo* d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  const int64_t chunks = N * K / 16;
+  int64_t blocks = (chunks + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(d->sms) * 8;
+  if (blocks > cap) blocks = cap;
+  fp6_to_tc_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(w6), chunks, static_cast<uint8_t*>(w6_tc), sfb, (N / 128) * (K / 128), sfb_tc);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fp6_to_tc launch");
+  return LTXFP8_OK;
+}
+
 int ltxfp8_dequantize_1x128(const void* q, const float* scales, int64_t row_stride, int64_t col_stride, int64_t M,
                             int64_t K, void* out, void* stream) {
   if (M < 0 || K <= 0 || K % 128 != 0) return fail(LTXFP8_ERR_UNSUPPORTED_SHAPE, "dequantize: K must be a positive multiple of 128");
@@ -807,7 +828,8 @@ int ltxfp8_gelu_tanh_quantize_1x128(const void* x, int64_t M, int64_t K, int64_t
 // the caller's workspace.
 static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
                      const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue& e,
-                     int64_t row0, int64_t rows, const SplitPlan* split, bool use_pair, cudaStream_t stream) {
+                     int64_t row0, int64_t rows, const SplitPlan* split, bool use_pair, cudaStream_t stream,
+                     bool w_fp6 = false) {
   const bool write_d = !e.skip_d;
   const bool lora = e.lora_ax != nullptr;
   const int tile_m = use_pair ? pair::kTileM : kBM;
@@ -818,7 +840,10 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
   CUtensorMap ma, mb, mlx, mlb;
   int rc = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_rows, K, rows, K, kBK, kBM);
   if (rc) return rc;
-  rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, w_rows_per_load);
+  if (w_fp6)  // 6-bit codes: K elements in K * 3 / 4 bytes per row
+    rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B, W, K, N, K / 4 * 3, kBK, w_rows_per_load);
+  else
+    rc = make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, K, N, K, kBK, w_rows_per_load);
   if (rc) return rc;
   if (lora) {
     const auto* lx_rows = static_cast<const __nv_bfloat16*>(e.lora_ax) + row0 * e.lora_r;
@@ -861,7 +886,7 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
   p.lora_alpha = e.lora_alpha;
   p.flags = (bias ? kGemmBias : 0) | (write_d ? kGemmWriteD : 0) | (lora ? kGemmLora : 0) |
             (e.gelu_tanh == LTXFP8_GELU_TANH_FAST ? kGemmGeluFast : 0) |
-            (e.requant_mode == LTXFP8_QUANT_TRITON ? kGemmRequantTriton : 0);
+            (e.requant_mode == LTXFP8_QUANT_TRITON ? kGemmRequantTriton : 0) | (w_fp6 ? kGemmWeightFp6 : 0);
   p.k_splits = 1;
   p.kb_per_split = p.num_kb;
   p.ws = nullptr;
@@ -898,9 +923,9 @@ static int gemm_rows(DeviceInfo* d, const void* A, const float* sfa, int64_t sfa
   return gemm_launch_full<false, false>(d, ma, mb, mlx, mlb, md, mq, p, stream);
 }
 
-int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
-                const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
-                void* stream) {
+static int gemm_entry(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                      const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
+                      void* stream, bool w_fp6) {
   ltxfp8_epilogue none;
   memset(&none, 0, sizeof(none));
   const ltxfp8_epilogue& e = ep ? *ep : none;
@@ -914,6 +939,7 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   if (write_d && !D) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: D is null");
   if (!write_d && !e.requant_q) return fail(LTXFP8_ERR_INVALID_ARGUMENT, "gemm: skip_d needs requant_q");
   if (!aligned(A, 16) || !aligned(W, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: A and W must be 16-byte aligned");
+  if (w_fp6 && !aligned(W, 32)) return fail(LTXFP8_ERR_MISALIGNED, "gemm_fp6w: W must be 32-byte aligned");
   if (write_d && !aligned(D, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: D must be 16-byte aligned");
   if (!aligned(sfa, 4) || !aligned(sfb, 4)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: scales must be 4-byte aligned");
   if (bias && !aligned(bias, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: bias must be 16-byte aligned");
@@ -939,19 +965,33 @@ int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, 
   // Default: the one-CTA kernel.  The CTA-pair kernel (256-row tiles over two
   // SMs) is selected explicitly; it halves the W bytes each SM streams but is
   // not yet faster on the FFN shapes.
+  // 6-bit weights run on the one-CTA kernel only.
   auto s = static_cast<cudaStream_t>(stream);
-  const bool use_pair = g_gemm_variant.load() == 2;
+  const bool use_pair = !w_fp6 && g_gemm_variant.load() == 2;
   if (use_pair) return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, true, s);
   const GemmPlan g = gemm_plan(d->sms, M, N, K);
   const size_t need = splitk_bytes(g);
   if (need == 0 || !e.workspace || need > e.workspace_bytes)
-    return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, false, s);
+    return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, M, nullptr, false, s, w_fp6);
   if (!aligned(e.workspace, 16)) return fail(LTXFP8_ERR_MISALIGNED, "gemm: workspace must be 16-byte aligned");
   if (g.split_row0 > 0) {
-    rc = gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, g.split_row0, nullptr, false, s);
+    rc = gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, 0, g.split_row0, nullptr, false, s, w_fp6);
     if (rc) return rc;
   }
-  return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, g.split_row0, M - g.split_row0, &g.split, false, s);
+  return gemm_rows(d, A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, e, g.split_row0, M - g.split_row0, &g.split, false, s,
+                   w_fp6);
+}
+
+int ltxfp8_gemm(const void* A, const float* sfa, int64_t sfa_ld, const void* W, const float* sfb,
+                const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
+                void* stream) {
+  return gemm_entry(A, sfa, sfa_ld, W, sfb, bias, D, M, N, K, ep, stream, false);
+}
+
+int ltxfp8_gemm_fp6w(const void* A, const float* sfa, int64_t sfa_ld, const void* W6, const float* sfb6,
+                     const float* bias, void* D, int64_t M, int64_t N, int64_t K, const ltxfp8_epilogue* ep,
+                     void* stream) {
+  return gemm_entry(A, sfa, sfa_ld, W6, sfb6, bias, D, M, N, K, ep, stream, true);
 }
 
 int ltxfp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes) {

@@ -209,6 +209,13 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, uint32_t m
          | ((m >> 4) << 24);            // M >> 4
 }
 
+// kind::f8f6f4 operand formats (instruction descriptor bits 7-9 for A, 10-12 for B).
+constexpr uint32_t kFmtE4M3 = 0u;
+constexpr uint32_t kFmtE2M3 = 3u;
+__host__ __device__ constexpr uint32_t with_b_format(uint32_t idesc, uint32_t fmt) {
+  return (idesc & ~(7u << 10)) | (fmt << 10);
+}
+
 // ---------------------------------------------------------------- cp.async (4-byte scale prefetch)
 __device__ __forceinline__ void cp_async_4(uint32_t smem_dst, const void* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_dst), "l"(gmem_src) : "memory");

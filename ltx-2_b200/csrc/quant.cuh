@@ -370,4 +370,52 @@ __global__ void __launch_bounds__(256) fp6_unpack_kernel(const uint8_t* __restri
   }
 }
 
+// Packed FP6 weight -> the tensor core's 6-bit order, and its scales -> x 2^-6.
+// A 6-bit code (s, e1, e0, m2, m1, m0) of the packing above is, read as e2m3
+// (bias 1), 2^6 times the e4m3 value it stands for (bias 7, top exponent bits 0;
+// subnormals alike), so codes read as e2m3 with scales x 2^-6 give the same
+// products.  The layout: every 16 codes of a row fill 12 bytes, code i at bits
+// 6i .. 6i+5 of their little-endian 96-bit word (the packing above fills 3 bytes
+// per 4 codes most-significant first).  One thread per 16 codes.
+__global__ void __launch_bounds__(256) fp6_to_tc_kernel(const uint8_t* __restrict__ x, int64_t chunks,
+                                                        uint8_t* __restrict__ out, const float* __restrict__ sfb,
+                                                        int64_t n_scales, float* __restrict__ sfb_out) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int64_t c = tid; c < chunks; c += stride) {
+    const uint32_t* in = reinterpret_cast<const uint32_t*>(x + c * 12);
+    const uint32_t i0 = __ldg(in), i1 = __ldg(in + 1), i2 = __ldg(in + 2);
+    uint8_t b[12];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      b[k] = static_cast<uint8_t>(i0 >> (8 * k));
+      b[4 + k] = static_cast<uint8_t>(i1 >> (8 * k));
+      b[8 + k] = static_cast<uint8_t>(i2 >> (8 * k));
+    }
+    uint64_t lo = 0, hi = 0;  // bits 0-63 and 64-95 of the output word
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t p = (static_cast<uint32_t>(b[3 * g]) << 16) | (static_cast<uint32_t>(b[3 * g + 1]) << 8) | b[3 * g + 2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t v6 = (p >> (18 - 6 * i)) & 0x3Fu;
+        const int bit = 6 * (4 * g + i);
+        if (bit + 6 <= 64) {
+          lo |= v6 << bit;
+        } else if (bit >= 64) {
+          hi |= v6 << (bit - 64);
+        } else {
+          lo |= v6 << bit;
+          hi |= v6 >> (64 - bit);
+        }
+      }
+    }
+    uint32_t* o = reinterpret_cast<uint32_t*>(out + c * 12);
+    o[0] = static_cast<uint32_t>(lo);
+    o[1] = static_cast<uint32_t>(lo >> 32);
+    o[2] = static_cast<uint32_t>(hi);
+  }
+  for (int64_t i = tid; i < n_scales; i += stride) sfb_out[i] = sfb[i] * 0.015625f;
+}
+
 }  // namespace ltxfp8

@@ -79,6 +79,7 @@ SIGNATURES = {
     "ltxfp8_quantize_weight_128x128": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _vp]),
     "ltxfp8_dequantize_1x128": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "ltxfp8_gemm": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.POINTER(Epilogue), _vp]),
+    "ltxfp8_gemm_fp6w": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.POINTER(Epilogue), _vp]),
     "ltxfp8_lora_a": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ltxfp8_gemm_set_variant": (_i32, [_i32]),
     "ltxfp8_gemm_workspace_bytes": (_i32, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
@@ -97,6 +98,7 @@ SIGNATURES = {
     "ltxfp8_quantize_weight_128x128_scaled": (_i32, [_vp, _i32, _i64, _i64, _f32, _vp, _vp, _vp]),
     "ltxfp8_fp6_pack": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "ltxfp8_fp6_unpack": (_i32, [_vp, _i64, _i64, _vp, _vp]),
+    "ltxfp8_fp6_to_tc": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "ltxfp8_gemm_static_scratch": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                            ctypes.POINTER(Epilogue), _vp]),
     "ltxfp8_device_status": (_i32, [ctypes.POINTER(ctypes.c_uint), _i32, _vp]),

@@ -45,6 +45,27 @@ def blockwise_fp8_gemm_fake(
     return torch.empty(a[0].shape[0], b[0].shape[0], dtype=torch.bfloat16, device=b[0].device)
 
 
+@torch.library.custom_op("blockwise::fp6_gemm", mutates_args=())
+def blockwise_fp6_gemm(
+    a: List[torch.Tensor],
+    b: List[torch.Tensor],
+    bias: Optional[torch.Tensor],
+) -> torch.Tensor:
+    """``blockwise::fp8_gemm`` with a 6-bit weight ``b = (w6_tc, sfb6)`` from
+    ``ops.fp6_to_tc``: the tensor core reads the packed codes directly.  No
+    reference counterpart (the reference unpacks to e4m3 first, linear.py:244-250)."""
+    return ops.gemm(a[0], a[1], b[0], b[1], bias, w_fp6=True)
+
+
+@blockwise_fp6_gemm.register_fake
+def blockwise_fp6_gemm_fake(
+    a: List[torch.Tensor],
+    b: List[torch.Tensor],
+    bias: Optional[torch.Tensor],
+) -> torch.Tensor:
+    return torch.empty(a[0].shape[0], b[0].shape[0], dtype=torch.bfloat16, device=b[0].device)
+
+
 def is_16bit(x) -> bool:
     return x.dtype == torch.float16 or x.dtype == torch.bfloat16
 
@@ -133,8 +154,17 @@ class BlockwiseFP8Linear(BlockwiseLinear):
 
 class BlockwiseFP6Linear(BlockwiseLinear):
     """FP6-range weights stored 6-bit packed ``[out, in*3/4]`` uint8 with fp32 128x128
-    block scales ``[out/128, in/128]`` (linear.py:212-284).  The forward pass unpacks
-    the codes to e4m3 (the dropped exponent bits are zero) and runs the FP8 GEMM."""
+    block scales ``[out/128, in/128]`` (linear.py:212-284).
+
+    The reference's forward unpacks the codes to an e4m3 weight and runs the FP8 GEMM
+    (linear.py:244-250).  Here the forward rewrites the packed codes into the tensor
+    core's 6-bit order (``ops.fp6_to_tc``, same size) and the GEMM streams them at 6
+    bits per element as e2m3 operands, with identical results.  ``keep_tc_weight``
+    (default False) keeps that copy between calls (0.75 byte per weight element more
+    memory, no per-call rewrite); ``weight`` and ``weight_scale`` stay in the
+    reference's layout either way.  ``fp8weight`` still gives the unpacked e4m3 codes."""
+
+    keep_tc_weight: bool = False
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None, dtype=None):
         assert in_features % 8 == 0, f"in_features must be divisible by 8 for fp6_pack, got {in_features}"
@@ -151,6 +181,26 @@ class BlockwiseFP6Linear(BlockwiseLinear):
     def fp8weight(self):
         from .functional import fp6_unpack_tensor
         return fp6_unpack_tensor(self.weight, self.in_features).view(torch.float8_e4m3fn)
+
+    def tc_weight(self):
+        """``(w6_tc, sfb6)``: the weight in the tensor core's 6-bit order and its scales
+        x 2^-6, cached while ``keep_tc_weight`` is set and the parameters are unchanged."""
+        key = (self.weight.data_ptr(), self.weight._version, self.weight_scale.data_ptr(),
+               self.weight_scale._version)
+        cached = self.__dict__.get("_tc_cache")
+        if self.keep_tc_weight and cached is not None and cached[0] == key:
+            return cached[1]
+        tc = ops.fp6_to_tc(self.weight, self.weight_scale)
+        self.__dict__["_tc_cache"] = (key, tc) if self.keep_tc_weight else None
+        return tc
+
+    def forward(self, x):
+        a = x if isinstance(x, tuple) else (x, None)
+        if is_16bit(a[0]):
+            a = blockwise_quantize_triton(a[0])
+        b, n, h = a[0].shape
+        d = blockwise_fp6_gemm([a[0].view(-1, h), a[1]], list(self.tc_weight()), self.bias)
+        return d.view(b, n, self.out_features)
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, transform_weights=True):

@@ -153,6 +153,35 @@ def fp6_unpack(x: torch.Tensor, original_n: int) -> torch.Tensor:
     return out
 
 
+def fp6_to_tc(w6: torch.Tensor, sfb: torch.Tensor, out: Optional[torch.Tensor] = None,
+              out_scales: Optional[torch.Tensor] = None):
+    """Packed FP6 weight uint8 [N, K*3/4] (:func:`fp6_pack`'s layout) and its fp32
+    scales [N/128, K/128] -> ``(w6_tc, sfb6)`` for ``gemm(..., w_fp6=True)``: the codes
+    in the tensor core's 6-bit order and the scales x 2^-6."""
+    _require_cuda("fp6_to_tc", w6, sfb)
+    if w6.dim() != 2 or w6.dtype != torch.uint8 or w6.shape[1] % 3:
+        raise RuntimeError("fp6_to_tc: expected a packed uint8 [N, K*3/4] weight")
+    N, K = w6.shape[0], w6.shape[1] // 3 * 4
+    if N % 128 or K % 128:
+        raise RuntimeError(f"fp6_to_tc: N and K must be multiples of 128 (N={N} K={K})")
+    if sfb.dtype != torch.float32 or tuple(sfb.shape) != (N // 128, K // 128):
+        raise RuntimeError(f"fp6_to_tc: scales must be fp32 [{N // 128}, {K // 128}]")
+    w6 = w6.contiguous()
+    sfb = sfb.contiguous()
+    if out is None:
+        out = torch.empty_like(w6)
+    if out_scales is None:
+        out_scales = torch.empty_like(sfb)
+    if out.shape != w6.shape or out.dtype != torch.uint8 or not out.is_contiguous() or out.data_ptr() % 32:
+        raise RuntimeError("fp6_to_tc: out must be a contiguous, 32-byte aligned uint8 tensor of the weight's shape")
+    if out_scales.shape != sfb.shape or out_scales.dtype != torch.float32 or not out_scales.is_contiguous():
+        raise RuntimeError("fp6_to_tc: out_scales must be contiguous fp32 of the scales' shape")
+    with _DeviceGuard(w6):
+        L.check(L.load().ltxfp8_fp6_to_tc(w6.data_ptr(), sfb.data_ptr(), N, K, out.data_ptr(),
+                                          out_scales.data_ptr(), _stream(w6)))
+    return out, out_scales
+
+
 def dequantize_1x128(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     """e4m3 [M, K] + scales (M, K/128) with any strides -> bf16 [M, K]."""
     _require_cuda("dequantize_1x128", q, scales)
@@ -361,7 +390,8 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
          bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,
          gelu=False, requant: bool = False, write_d: bool = True,
          lora_ax: Optional[torch.Tensor] = None, lora_b: Optional[torch.Tensor] = None,
-         lora_alpha: float = 1.0, split_k: bool = True, requant_mode: int = L.QUANT_TORCH):
+         lora_alpha: float = 1.0, split_k: bool = True, requant_mode: int = L.QUANT_TORCH,
+         w_fp6: bool = False):
     """Blockwise FP8 GEMM with fused epilogue.
 
     ``gelu``: False, True (torch's GELU-tanh formula, bf16 results identical to
@@ -371,15 +401,21 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
     1x128 quantisation of the (GELU'd) bf16 output in the layout blockwise::quantize
     produces, with ``requant_mode``'s arithmetic (QUANT_TORCH or QUANT_TRITON).
     Skinny shapes get a split-K workspace from the caching allocator unless
-    ``split_k`` is False."""
+    ``split_k`` is False.  ``w_fp6``: ``w_q``/``sfb`` are a 6-bit weight from
+    :func:`fp6_to_tc` (uint8 [N, K*3/4]), read by the tensor core as e2m3."""
     _require_cuda("gemm", a_q, sfa, w_q, sfb, bias, lora_ax, lora_b)
     if a_q.dim() != 2 or w_q.dim() != 2:
         raise RuntimeError("gemm expects 2-D operands")
     M, K = a_q.shape
     N, K2 = w_q.shape
-    if K != K2:
+    if w_fp6:
+        if w_q.dtype != torch.uint8 or K2 * 4 != K * 3:
+            raise RuntimeError(f"gemm: a 6-bit weight must be uint8 [N, {K * 3 // 4}] from fp6_to_tc")
+        if w_q.data_ptr() % 32:
+            raise RuntimeError("gemm: a 6-bit weight must be 32-byte aligned")
+    elif K != K2:
         raise RuntimeError(f"gemm: K mismatch ({K} vs {K2})")
-    if a_q.dtype != torch.float8_e4m3fn or w_q.dtype != torch.float8_e4m3fn:
+    if a_q.dtype != torch.float8_e4m3fn or (not w_fp6 and w_q.dtype != torch.float8_e4m3fn):
         raise RuntimeError("gemm: operands must be float8_e4m3fn")
     if not a_q.is_contiguous() or not w_q.is_contiguous():
         raise RuntimeError("gemm: operands must be contiguous (K-major)")
@@ -441,9 +477,10 @@ def gemm(a_q: torch.Tensor, sfa: torch.Tensor, w_q: torch.Tensor, sfb: torch.Ten
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a_q.device)
             ep.workspace = ws.data_ptr()
             ep.workspace_bytes = ws_bytes
-        L.check(L.load().ltxfp8_gemm(a_q.data_ptr(), sfa.data_ptr(), ld, w_q.data_ptr(), sfb.data_ptr(),
-                                     None if bias is None else bias.data_ptr(),
-                                     None if d is None else d.data_ptr(), M, N, K, ep, _stream(a_q)))
+        fn = L.load().ltxfp8_gemm_fp6w if w_fp6 else L.load().ltxfp8_gemm
+        L.check(fn(a_q.data_ptr(), sfa.data_ptr(), ld, w_q.data_ptr(), sfb.data_ptr(),
+                   None if bias is None else bias.data_ptr(),
+                   None if d is None else d.data_ptr(), M, N, K, ep, _stream(a_q)))
     if requant:
         return d, q, s
     return d

@@ -284,6 +284,24 @@ def fp6_unpack(packed: np.ndarray, n: int) -> np.ndarray:
     return (((v & 0x20) << 2) | (v & 0x1F)).astype(np.uint8).reshape(packed.shape[0], n)
 
 
+def fp6_to_tc(packed: np.ndarray, n: int) -> np.ndarray:
+    """fp6_pack's layout -> the 6-bit operand layout of the tensor core (not a reference
+    function: the layout the TMA's 16 x 6-bit type and kind::f8f6f4's e2m3 operand
+    read): every 16 codes of a row in 12 bytes, code i at bits 6i..6i+5 of their
+    little-endian 96-bit word."""
+    m = packed.shape[0]
+    b = np.ascontiguousarray(packed, dtype=np.uint8).reshape(m, n // 4, 3).astype(np.uint32)
+    p = (b[..., 0] << 16) | (b[..., 1] << 8) | b[..., 2]
+    v = np.stack([(p >> 18) & 0x3F, (p >> 12) & 0x3F, (p >> 6) & 0x3F, p & 0x3F], axis=-1)
+    v = v.reshape(m, n // 16, 16).astype(np.uint64)
+    bits = np.zeros((m, n // 16, 96), dtype=np.uint8)
+    for i in range(16):
+        for j in range(6):
+            bits[..., 6 * i + j] = ((v[..., i] >> np.uint64(j)) & np.uint64(1)).astype(np.uint8)
+    out = np.packbits(bits.reshape(m, n // 16, 12, 8), axis=-1, bitorder="little")
+    return out.reshape(m, n * 3 // 4)
+
+
 def exp_cw(x: float) -> float:
     return float(lib().orc_exp_cw(x))
 

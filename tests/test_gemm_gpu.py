@@ -393,6 +393,28 @@ def test_tail_wave_split(cuda_device, M, N, K):
     assert diff <= 0.02 * dl1.float().abs().max().item()
 
 
+@pytest.mark.parametrize("M,N,K", [(6000, 2304, 16384), (8000, 6144, 8192)])
+def test_long_k_ragged_shapes(cuda_device, M, N, K):
+    """Long K (8192, 16384) with ragged M and an odd number of 256-column tiles (2304 =
+    9 x 256), several M groups of the rasterisation: bias and the fused GELU + requant
+    against the oracle on a sample of rows, and deterministic."""
+    from ltx_kernels.blockwise import ops
+    x, aq, asc, wq, wsc, b = _problem(M, N, K, cuda_device, seed=N + K)
+    d = ops.gemm(aq, asc, wq, wsc, b, split_k=False)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.arange(0, M, max(1, M // 48)), [M - 129, M - 128, M - 1]]))
+    ri = torch.from_numpy(rows).to(cuda_device)
+    ref = O.gemm_dequant_f32(bits(aq[ri]), scales_mn(asc, M)[:, rows], bits(wq), wsc.cpu().numpy(), b.cpu().numpy())
+    _check(d[ri], ref)
+    assert torch.equal(d, ops.gemm(aq, asc, wq, wsc, b, split_k=False))
+    _, q, s = ops.gemm(aq, asc, wq, wsc, b, gelu=True, requant=True, write_d=True, split_k=False)
+    dg = ops.gemm(aq, asc, wq, wsc, b, gelu=True, split_k=False)
+    torch.cuda.synchronize()
+    oq, os_ = O.quant_act_1x128(bits(dg[ri]))
+    assert O.codes_equal(bits(q[ri]), oq).all()
+    assert O.scales_equal(scales_mn(s, M)[:, rows], os_[:, : len(rows)]).all()
+
+
 # --------------------------------------------------------------------------- staged epilogue
 @pytest.mark.parametrize("M,N,K", [(37, 384, 512), (130, 640, 256), (1, 128, 128), (300, 1152, 1024)])
 @pytest.mark.parametrize("gelu,requant,write_d", [(False, False, True), (True, False, True), (False, True, True),

@@ -172,3 +172,16 @@ def test_fp6_pack_roundtrip_and_layout():
     w = np.random.default_rng(1).normal(0, 0.02, (128, 256)).astype(np.float32)
     q, s = O.quant_weight_128x128(w, 0.1172)
     assert ((q & 0x60) == 0).all()                                 # the FP6 quantiser never sets them
+
+
+def test_fp6_to_tc_layout():
+    """The tensor core's 6-bit order on a hand-built group: codes 0..15 (6-bit values
+    equal to the e4m3 codes below 32) land at bits 6i of a little-endian 96-bit word;
+    a sign bit (e4m3 bit 7) lands at bit 6i + 5."""
+    c = np.arange(128, dtype=np.uint8).reshape(1, 128) % 16
+    c[0, 16] |= 0x80
+    tc = O.fp6_to_tc(O.fp6_pack(c), 128)
+    assert tc.shape == (1, 96)
+    word = sum(i << (6 * i) for i in range(16))
+    assert tc[0, :12].tolist() == list(word.to_bytes(12, "little"))
+    assert tc[0, 12:24].tolist() == list((word | (1 << 5)).to_bytes(12, "little"))
