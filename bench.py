@@ -1125,8 +1125,9 @@ def run_fp6(args, rank: int, world: int, local: int):
     flush = L2Flush(dev)
     g = torch.Generator(device=dev).manual_seed(11)
     points, launches = [], 0
+    shapes = [sh for sh in FP6_SHAPES if not args.m or sh[0] == args.m]   # --m: one token count only
     clk = ClockSampler(local).start()
-    for M, K, N in FP6_SHAPES:
+    for M, K, N in shapes:
         w = torch.randn(N, K, generator=g, device=dev) * 0.02
         wq, ws = ops.quantize_weight_128x128(w, scale_max=0.1172)
         del w
@@ -1169,7 +1170,7 @@ def run_fp6(args, rank: int, world: int, local: int):
         "n_gpus": 1, "steps": 1, "warmup": 3, "ms_per_step": tot / 1e3, "higher_is_better": True,
         "scaling": "none", "vs_baseline": None, "dtype": "e4m3 x e2m3 (6-bit) -> f32 accumulate, bf16 out",
         "data": "synthetic (seeded; FP6-range weights from the 0.1172 quantiser)",
-        "config": {"workload": "BlockwiseFP6Linear GEMM shapes", "shapes": [list(x) for x in FP6_SHAPES],
+        "config": {"workload": "BlockwiseFP6Linear GEMM shapes", "shapes": [list(x) for x in shapes],
                    "l2": "flushed between launches when the working set fits in L2"},
         "peaks": {"hbm_gbs": bw, "hbm_source": bw_src}, "points": points, "e2e": None, "cpu_baseline": None,
         "gpu_launches": launches, "clocks": c}))
