@@ -192,11 +192,38 @@ def _events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def time_launches(fn, reps: int, warmup: int = 3, flush=None):
+def graphed(fn):
+    """`fn` captured once as a CUDA graph; returns the replay callable, or None when `fn`
+    cannot be captured.  One replay is one host call, so events around short kernels hold
+    their device time rather than the Python per-call overhead (a one-row quantisation
+    times at 9 us eager after an L2 flush, 24 us eager back to back)."""
+    import torch
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+    except Exception as e:  # noqa: BLE001 -- reported, then timed eagerly
+        torch.cuda.synchronize()
+        print(f"bench: graph capture failed ({type(e).__name__}: {e}); timing eager calls", file=sys.stderr)
+        return None
+    return g.replay
+
+
+def time_launches(fn, reps: int, warmup: int = 3, flush=None, graph: bool = False):
     """Mean device time (ms) of `fn` over `reps` launches, each bracketed by CUDA events on
-    the current stream; `flush()` (untimed) runs before each launch when given."""
+    the current stream; `flush()` (untimed) runs before each launch when given.  `graph`:
+    time replays of `fn` captured as a CUDA graph (falls back to eager calls when the
+    capture fails)."""
     import torch
     for _ in range(warmup):
+        fn()
+    if graph:
+        fn = graphed(fn) or fn
         fn()
     evs = [_events() for _ in range(reps)]
     for s, e in evs:
@@ -1066,7 +1093,7 @@ def run_sweep(args, rank: int, world: int, local: int):
             aq, asc = ops.quantize_1x128(synth_acts(M, K, g, dev))
             small = M * K + N * K + 2 * M * N < (126 << 20)
             f = lambda: ops.gemm(aq, asc, wq, ws, b)
-            ms = time_launches(f, 20 if M <= 2048 else 8, flush=flush if small else None)
+            ms = time_launches(f, 20 if M <= 2048 else 8, flush=flush if small else None, graph=True)
             fl, by = 2.0 * M * N * K, gemm_alg_bytes(M, K, N, "bias")
             ai = fl / by
             bound = "hbm" if ai < ridge else "tensor"
@@ -1078,7 +1105,7 @@ def run_sweep(args, rank: int, world: int, local: int):
                 def ref():
                     d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
                     G.fp8_gemm_nt_sm89((aq, asc), (wq, ws), d, b, use_fast_accum=False)
-                rms = time_launches(ref, 5 if M <= 2048 else 3, warmup=1, flush=flush if small else None)
+                rms = time_launches(ref, 5 if M <= 2048 else 3, warmup=1, flush=flush if small else None, graph=True)
                 p["ref_sm89_ms"], p["speedup_vs_sm89"] = rms, rms / ms
             points.append(p)
             tot_fl += fl
@@ -1091,7 +1118,8 @@ def run_sweep(args, rank: int, world: int, local: int):
         "unit": "TFLOP/s", "n_gpus": 1, "steps": 1, "warmup": 3, "ms_per_step": tot_ms, "higher_is_better": True,
         "scaling": "none", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 accumulate, bf16 out",
         "data": "synthetic (seeded; BASELINE.json distributions)",
-        "config": {"workload": "config-4 roofline sweep", "M": list(SWEEP_M), "KN": [list(k) for k in SWEEP_KN]},
+        "config": {"workload": "config-4 roofline sweep", "M": list(SWEEP_M), "KN": [list(k) for k in SWEEP_KN],
+                   "timing": "CUDA-graph replays of each call between CUDA events"},
         "peaks": {"fp8_tflops": pk, "fp8_source": pk_src, "hbm_gbs": bw, "hbm_source": bw_src,
                   "ridge_flop_per_byte": ridge},
         "points": points, "e2e": None, "cpu_baseline": None, "gpu_launches": sum(p["launches"] for p in points) * 8,
@@ -1141,11 +1169,12 @@ def run_fp6(args, rank: int, world: int, local: int):
         d6 = ops.gemm(aq, asc, tc, s6, b, w_fp6=True)
         d8 = ops.gemm(aq, asc, ops.fp6_unpack(w6, K).view(torch.float8_e4m3fn), ws, b)
         same = bool(torch.equal(d6, d8))
-        t_tc = time_launches(lambda: ops.gemm(aq, asc, tc, s6, b, w_fp6=True), reps, flush=fl)
-        t_tr = time_launches(lambda: ops.gemm(aq, asc, *ops.fp6_to_tc(w6, ws), b, w_fp6=True), reps, flush=fl)
+        t_tc = time_launches(lambda: ops.gemm(aq, asc, tc, s6, b, w_fp6=True), reps, flush=fl, graph=True)
+        t_tr = time_launches(lambda: ops.gemm(aq, asc, *ops.fp6_to_tc(w6, ws), b, w_fp6=True), reps, flush=fl,
+                             graph=True)
         t_un = time_launches(lambda: ops.gemm(aq, asc, ops.fp6_unpack(w6, K).view(torch.float8_e4m3fn), ws, b),
-                             reps, flush=fl)
-        t_f8 = time_launches(lambda: ops.gemm(aq, asc, wq, ws, b), reps, flush=fl)
+                             reps, flush=fl, graph=True)
+        t_f8 = time_launches(lambda: ops.gemm(aq, asc, wq, ws, b), reps, flush=fl, graph=True)
         launches += reps * (2 * ops.gemm_plan(M, N, K, dev)["launches"] + 2) * 2
         by = M * K + 4 * M * K // 128 + N * K * 3 // 4 + 4 * (N // 128) * (K // 128) + 4 * N + 2 * M * N
         p = {"M": M, "K": K, "N": N, "bit_identical_to_unpack_fp8": same,
@@ -1158,7 +1187,7 @@ def run_fp6(args, rank: int, world: int, local: int):
                 w8 = R.fp6_unpack(w6, K).view(torch.float8_e4m3fn)
                 d = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
                 G.fp8_gemm_nt_sm89((aq, asc), (w8, ws), d, b, use_fast_accum=False)
-            p["ref_unpack_sm89_us"] = time_launches(ref, 5 if M <= 2048 else 3, warmup=1, flush=fl) * 1e3
+            p["ref_unpack_sm89_us"] = time_launches(ref, 5 if M <= 2048 else 3, warmup=1, flush=fl, graph=True) * 1e3
             p["speedup_tc_vs_ref"] = p["ref_unpack_sm89_us"] / p["fp6_tc_us"]
         points.append(p)
         del wq, ws, w6, tc, s6, aq, asc, d6, d8
@@ -1171,7 +1200,8 @@ def run_fp6(args, rank: int, world: int, local: int):
         "scaling": "none", "vs_baseline": None, "dtype": "e4m3 x e2m3 (6-bit) -> f32 accumulate, bf16 out",
         "data": "synthetic (seeded; FP6-range weights from the 0.1172 quantiser)",
         "config": {"workload": "BlockwiseFP6Linear GEMM shapes", "shapes": [list(x) for x in shapes],
-                   "l2": "flushed between launches when the working set fits in L2"},
+                   "l2": "flushed between launches when the working set fits in L2",
+                   "timing": "CUDA-graph replays of each call between CUDA events"},
         "peaks": {"hbm_gbs": bw, "hbm_source": bw_src}, "points": points, "e2e": None, "cpu_baseline": None,
         "gpu_launches": launches, "clocks": c}))
 
