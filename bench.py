@@ -738,23 +738,81 @@ def run_dit(args, rank: int, world: int, local: int):
     hosts = {key: x.cpu().pin_memory() for key, x in xin.items()}
     last = run_step()
     out_host = {c: torch.empty(t.shape, dtype=t.dtype).pin_memory() for c, t in last.items()}
-
-    def e2e_step():
-        for key, h in hosts.items():
-            xin[key].copy_(h, non_blocking=True)
-        o = run_step()
-        for c, t in o.items():
-            out_host[c].copy_(t, non_blocking=True)
-
-    e2e_step()
-    barrier()
-    e0, e1 = _events()
     e2e_steps = max(1, min(args.steps, 3))
-    e0.record()
-    for _ in range(e2e_steps):
+    if graph is not None:
+        # Double-buffered, as a serving loop runs it: a second set of input buffers and
+        # a second capture of the step reading them (sharing the first graph's memory
+        # pool: the two never run at once), so step i+1's H2D (one copy stream) and
+        # step i's D2H (another) overlap step i's compute.  Every step's copies stay
+        # inside the timed region: the first H2D and the last D2H are exposed.
+        xin_a = dict(xin)
+        xin_b = {key: torch.empty_like(x) for key, x in xin.items()}
+        xin.update(xin_b)
+        graph_b = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_b, pool=graph.pool()):
+            outs_b = step()
+        xin.update(xin_a)
+        sets = [(xin_a, graph, outs), (xin_b, graph_b, outs_b)]
+        main = torch.cuda.current_stream(dev)
+        h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+        def e2e_run(n):
+            ev_in = [torch.cuda.Event() for _ in range(2)]
+            ev_done = [torch.cuda.Event() for _ in range(2)]
+            ev_out = [torch.cuda.Event() for _ in range(2)]
+            used = [False, False]
+            with torch.cuda.stream(h2d_s):
+                h2d_s.wait_stream(main)
+                for key, h in hosts.items():
+                    sets[0][0][key].copy_(h, non_blocking=True)
+                ev_in[0].record(h2d_s)
+            for i in range(n):
+                cur, nxt = i % 2, (i + 1) % 2
+                if i + 1 < n:
+                    with torch.cuda.stream(h2d_s):
+                        if used[nxt]:
+                            h2d_s.wait_event(ev_done[nxt])  # the step that last read these inputs
+                        for key, h in hosts.items():
+                            sets[nxt][0][key].copy_(h, non_blocking=True)
+                        ev_in[nxt].record(h2d_s)
+                main.wait_event(ev_in[cur])
+                if used[cur]:
+                    main.wait_event(ev_out[cur])  # its outputs of two steps ago are copied out
+                sets[cur][1].replay()
+                ev_done[cur].record(main)
+                used[cur] = True
+                with torch.cuda.stream(d2h_s):
+                    d2h_s.wait_event(ev_done[cur])
+                    for c, t in sets[cur][2].items():
+                        out_host[c].copy_(t, non_blocking=True)
+                    ev_out[cur].record(d2h_s)
+            main.wait_stream(d2h_s)
+            main.wait_stream(h2d_s)
+
+        e2e_run(2)
+        barrier()
+        e0, e1 = _events()
+        e0.record()
+        e2e_run(e2e_steps)
+        e1.record()
+        barrier()
+        del graph_b, outs_b, sets
+    else:
+        def e2e_step():
+            for key, h in hosts.items():
+                xin[key].copy_(h, non_blocking=True)
+            o = run_step()
+            for c, t in o.items():
+                out_host[c].copy_(t, non_blocking=True)
+
         e2e_step()
-    e1.record()
-    barrier()
+        barrier()
+        e0, e1 = _events()
+        e0.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record()
+        barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     assert ops.device_status() == 0
     if world > 1:
@@ -794,7 +852,9 @@ def run_dit(args, rank: int, world: int, local: int):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "H2D of the step's bf16 token streams into the step's input buffers, "
                            "torch.ops.blockwise.quantize + BlockwiseFP8Linear / BlockwiseFP8FeedForward "
-                           "(graph-replayed), D2H of the last block's video and audio outputs"},
+                           "(graph-replayed), D2H of the last block's video and audio outputs"
+                           + ("; double-buffered inputs, the next step's H2D and this step's D2H on copy "
+                              "streams overlapping its compute" if not args.no_graph else "")},
             "gpu_launches": args.steps * launches,
             "cuda_graph": not args.no_graph,
             "clocks": clk,
