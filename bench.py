@@ -738,7 +738,7 @@ def run_dit(args, rank: int, world: int, local: int):
     hosts = {key: x.cpu().pin_memory() for key, x in xin.items()}
     last = run_step()
     out_host = {c: torch.empty(t.shape, dtype=t.dtype).pin_memory() for c, t in last.items()}
-    e2e_steps = max(1, min(args.steps, 3))
+    e2e_steps = max(1, min(args.steps, 10))
     if graph is not None:
         # Double-buffered, as a serving loop runs it: a second set of input buffers and
         # a second capture of the step reading them (sharing the first graph's memory
