@@ -100,3 +100,32 @@ def test_fake_tensor_shapes():
         w = torch.empty(384, 256, dtype=torch.float8_e4m3fn)
         d = torch.ops.blockwise.fp8_gemm([a, s], [w, torch.empty(3, 2)], None, False)
         assert d.shape == (10, 384) and d.dtype == torch.bfloat16
+
+
+def test_fp6_entry_points_reject_bad_arguments_without_device():
+    """The 6-bit weight path validates before touching a device: shapes, null pointers,
+    the tensor-core copy's 32-byte alignment and the GEMM's shape rules."""
+    from ltx_kernels import _lib
+    L = _lib.load()
+    assert L.ltxfp8_fp6_to_tc(16, 16, 100, 128, 32, 16, None) == _lib.ERR_UNSUPPORTED_SHAPE
+    assert L.ltxfp8_fp6_to_tc(None, 16, 128, 128, 32, 16, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.ltxfp8_fp6_to_tc(16, 16, 128, 128, 48, 16, None) == _lib.ERR_MISALIGNED
+    assert "fp6_to_tc" in L.ltxfp8_last_error().decode()
+    assert L.ltxfp8_gemm_fp6w(16, 16, 128, 32, 16, None, 16, 128, 100, 256, None, None) == _lib.ERR_UNSUPPORTED_SHAPE
+    assert L.ltxfp8_gemm_fp6w(16, 16, 128, 48, 16, None, 16, 128, 256, 256, None, None) == _lib.ERR_MISALIGNED
+
+
+def test_fp6_linear_keeps_the_reference_parameters():
+    """BlockwiseFP6Linear's state dict is the reference's (linear.py:212-243): the packed
+    uint8 weight [out, in*3/4], fp32 block scales and bias; the tensor-core copy of the
+    weight is never a parameter or buffer, and it is kept only on request."""
+    import ltx_kernels.blockwise  # noqa: F401
+    from ltx_kernels.blockwise import BlockwiseFP6Linear
+    layer = BlockwiseFP6Linear(1024, 512, bias=True, device="cpu")
+    sd = layer.state_dict()
+    assert sorted(sd) == ["bias", "weight", "weight_scale"]
+    assert sd["weight"].shape == (512, 768) and sd["weight"].dtype == torch.uint8
+    assert sd["weight_scale"].shape == (4, 8) and sd["weight_scale"].dtype == torch.float32
+    assert sd["bias"].dtype == torch.float32
+    assert layer.keep_tc_weight is False
+    assert "blockwise::fp6_gemm" in str(torch.ops.blockwise.fp6_gemm.default._schema)
